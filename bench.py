@@ -1,0 +1,434 @@
+#!/usr/bin/env python
+"""Benchmark of the torch.ops.kp hot path on B200s: prints ONE JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload KEY] [--impl ours|reference]
+
+A step is one call of the op on one full-size synthetic instance of the workload
+(default: full sum of 2^28+1 fp32 values drawn U(-1,1), the reduction headline
+configuration). Under torchrun each rank is one GPU holding its own instance (weak
+scaling: the job is N instances); ops whose math needs an exchange step run it over
+NCCL inside the timed step (reduce_sum: all_reduce of the fp32 partials).
+
+value      whole-job algorithmic bytes (or FLOPs) / max-over-ranks device time,
+           inputs resident in HBM; per-step CUDA events, L2 flushed between steps
+           when the working set fits in L2 (the flush is outside the events).
+e2e        the same metric through the public API (torch.ops.kp) with the inputs
+           copied from pinned host memory and the result copied back inside the
+           timed region.
+roofline   the op's algorithmic bytes/FLOPs per call over its measured device time,
+           against MEASURED_PEAKS.json (HBM copy GB/s, or cuBLAS bf16 TFLOP/s).
+cpu_baseline  the reference's CPU path (the PyTorch built-in its spec names as
+           ``baseline``) on this box's host cores, rank 0 at N=1 only.
+--impl reference  runs only that CPU path, on the same workload, and prints its line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+from kernelpilot_b200 import dist as kdist  # noqa: E402
+from kernelpilot_b200.specs import CONFIGS, Workload  # noqa: E402
+
+METRIC = json.loads((REPO / "BASELINE.json").read_text())["metric"] \
+    if (REPO / "BASELINE.json").exists() else \
+    "achieved HBM TB/s (softmax/reduce) and BF16 TFLOPS (GEMM/attn), % of peak"
+DEFAULT_WORKLOAD = "reduce_f32_2p28p1"
+L2_BYTES = 126 * 1024 * 1024
+# kernel launches of ours per op call (the op's level-1 kernel + finish, or one kernel)
+LAUNCHES_PER_CALL = {"reduce_sum": 2, "softmax": 1, "matmul": 1, "attention": 1,
+                     "attention_causal": 1}
+DTYPE_NAMES = {torch.float32: "f32", torch.float16: "f16", torch.bfloat16: "bf16"}
+
+
+# ------------------------------------------------------------------ helpers
+
+def work_per_call(w: Workload) -> float:
+    """Algorithmic bytes (hbm-bound) or FLOPs (tensor-bound) of one call."""
+    s = w.spec
+    return s.bytes_moved(w.shape, w.dtype) if w.bound == "hbm" else s.flops(w.shape)
+
+
+def unit_of(w: Workload) -> str:
+    return "TB/s" if w.bound == "hbm" else "TFLOPS"
+
+
+def rate(w: Workload, ms: float) -> float:
+    return work_per_call(w) / (ms / 1e3) / 1e12
+
+
+def measured_peaks() -> dict:
+    try:
+        return json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        return {}
+
+
+def roofline_peak(w: Workload) -> tuple[float, str]:
+    """(peak, where it came from) in GB/s or TFLOP/s."""
+    mp = measured_peaks()
+    if w.bound == "hbm":
+        if "hbm_gbs" in mp:
+            return float(mp["hbm_gbs"]), "measured"
+        return 6650.0, "fallback"
+    if "bf16_tflops" in mp:
+        return float(mp["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def profiled_traffic(w: Workload) -> float | None:
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary
+    (a line ``traffic_per_launch_bytes: <int>`` in profiles/<workload>.md)."""
+    p = REPO / "profiles" / f"{w.key}.md"
+    try:
+        m = re.search(r"traffic_per_launch_bytes:\s*([0-9]+)", p.read_text())
+    except OSError:
+        return None
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (getattr(self, "out", "") or "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9], strict=False):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def physical_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+# ------------------------------------------------------------------ op plumbing
+
+def make_step(w: Workload, inputs: tuple, rk: kdist.Rank):
+    """The timed unit: one call of the best variant (+ the exchange step, if any)."""
+    from kernelpilot_b200 import registry
+
+    fn = registry.best(w.kernel)
+    if w.kernel == "reduce_sum":
+        return lambda: kdist.sharded_reduce_sum(inputs[0], fn)
+    return lambda: fn(*inputs)
+
+
+def time_steps(step, steps: int, flush: bool, rk: kdist.Rank) -> tuple[float, list[float]]:
+    """(max-over-ranks total ms of the K steps, per-step ms on this rank)."""
+    from kernelpilot_b200.benchmark import flush_l2
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if rk.world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        if flush:
+            flush_l2()
+        starts[i].record()
+        step()
+        ends[i].record()
+    torch.cuda.synchronize()
+    if rk.world > 1:
+        torch.distributed.barrier()
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends, strict=True)]
+    total = torch.tensor([sum(per)], dtype=torch.float64, device="cuda")
+    if rk.world > 1:
+        torch.distributed.all_reduce(total, op=torch.distributed.ReduceOp.MAX)
+    return float(total.item()), per
+
+
+def time_e2e(w: Workload, dev_inputs: tuple, steps: int, rk: kdist.Rank) -> dict:
+    """Public API with host buffers: H2D of the step's inputs from pinned memory, the
+    op, D2H of its result, all inside the timed region."""
+    from kernelpilot_b200 import registry
+
+    fn = registry.best(w.kernel)
+    host = [t.cpu().pin_memory() for t in dev_inputs]
+    dev = [torch.empty_like(t) for t in dev_inputs]
+    out_host = None
+    h2d = sum(t.numel() * t.element_size() for t in host)
+
+    def one():
+        nonlocal out_host
+        for d, h in zip(dev, host, strict=True):
+            d.copy_(h, non_blocking=True)
+        if w.kernel == "reduce_sum":
+            r = kdist.sharded_reduce_sum(dev[0], fn)
+        else:
+            r = fn(*dev)
+        if out_host is None:
+            out_host = torch.empty(r.shape, dtype=r.dtype, pin_memory=True)
+        out_host.copy_(r, non_blocking=True)
+
+    one()
+    torch.cuda.synchronize()
+    total, _ = time_steps(one, steps, flush=False, rk=rk)
+    d2h = out_host.numel() * out_host.element_size()
+    ms = total / steps
+    return {"value": rate(w, ms) * rk.world, "unit": unit_of(w), "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms}
+
+
+# ------------------------------------------------------------------ CPU (reference) path
+
+def reference_baseline(w: Workload):
+    """(callable, kind): the reference's CPU implementation of this op.
+
+    Preferred: the unmodified reference package installed under baseline/_ref, its
+    ``spec.baseline`` (the PyTorch built-in, kernelpilot/specs.py:127,158,200,274).
+    Else the same built-in through this package's mirror of the spec.
+    """
+    ref_dir = REPO / "baseline" / "_ref"
+    if w.kernel == "attention_causal":
+        # the reference has no causal op; its attention baseline with the causal flag
+        import torch.nn.functional as F
+
+        return (lambda q, k, v: F.scaled_dot_product_attention(q, k, v, is_causal=True),
+                "reference")
+    if (ref_dir / "kernelpilot").exists():
+        sys.path.insert(0, str(ref_dir))
+        try:
+            from kernelpilot.specs import get_spec as ref_get_spec  # type: ignore
+
+            return ref_get_spec(w.kernel).baseline, "reference"
+        except ImportError:
+            pass
+    return w.spec.baseline, "reference"
+
+
+def cpu_sample(w: Workload) -> tuple[tuple, float, str]:
+    """A bounded CPU sample of the workload: (inputs, fraction of one call, label)."""
+    gen_cpu = torch.device("cpu")
+    if w.kernel == "reduce_sum":
+        return w.make_inputs(w.shape, w.dtype, gen_cpu, 0), 1.0, "the full instance"
+    if w.kernel == "softmax":
+        M, N = w.shape
+        rows = min(M, max(1, (64 << 20) // (N * 4)))
+        return w.make_inputs((rows, N), w.dtype, gen_cpu, 0), rows / M, f"{rows} of {M} rows"
+    if w.kernel == "matmul":
+        M, N, K = w.shape
+        rows = min(M, 512)
+        a, b = w.make_inputs((rows, N, K), w.dtype, gen_cpu, 0)
+        return (a, b), rows / M, f"{rows} of {M} rows of A"
+    B, H, S, D = w.shape
+    q, k, v = w.make_inputs((1, 1, S, D), w.dtype, gen_cpu, 0)
+    return (q, k, v), 1.0 / (B * H), f"1 of {B * H} (batch, head) slices"
+
+
+def time_cpu(w: Workload, reps: int, budget_s: float = 20.0) -> dict:
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    fn, kind = reference_baseline(w)
+    inputs, frac, label = cpu_sample(w)
+    fn(*inputs)
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(max(1, reps)):
+        t0 = time.perf_counter()
+        fn(*inputs)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    sec = statistics.median(times) / frac  # scaled to one full call
+    value = work_per_call(w) / sec / 1e12
+    return {"value": value, "unit": unit_of(w), "cores": torch.get_num_threads(),
+            "kind": kind, "sample": f"{label}, median of {len(times)} calls, "
+                                   f"scaled to one full call",
+            "ms_per_call": sec * 1e3}
+
+
+def run_reference(args, rk: kdist.Rank) -> int:
+    if rk.rank != 0:
+        return 0
+    w = CONFIGS[args.workload]
+    cb = time_cpu(w, reps=args.steps + args.warmup)
+    line = {"metric": METRIC, "value": cb["value"], "unit": cb["unit"], "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_call"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": DTYPE_NAMES[w.dtype], "data": "synthetic",
+            "config": {"workload": w.key, "shape": list(w.shape), "description": w.description},
+            "impl": "reference", "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ main
+
+def quick_measure(w: Workload, rk: kdist.Rank, steps: int = 10, warmup: int = 3) -> dict:
+    """Device-side rate of another workload on this GPU (for the configs table)."""
+    inputs = w.inputs("cuda", seed=0)
+    step = make_step(w, inputs, kdist.Rank(0, 1, rk.local_rank))
+    for _ in range(warmup):
+        step()
+    flush = sum(t.numel() * t.element_size() for t in inputs) < 2 * L2_BYTES
+    total, _ = time_steps(step, steps, flush, kdist.Rank(0, 1, rk.local_rank))
+    ms = total / steps
+    peak, src = roofline_peak(w)
+    val = rate(w, ms)
+    scale = 1e3 if w.bound == "hbm" else 1.0
+    del inputs
+    torch.cuda.empty_cache()
+    return {"value": round(val, 4), "unit": unit_of(w), "ms": round(ms, 5),
+            "frac_of_peak": round(val * scale / peak, 4), "peak_source": src}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(CONFIGS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the device-side table of the other headline workloads")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rk = kdist.env_rank()
+    if args.impl == "reference":
+        return run_reference(args, rk)
+
+    rk = kdist.init(timeout_s=300)
+    torch.cuda.set_device(rk.local_rank)
+    from kernelpilot_b200 import ext
+
+    if not ext.load():
+        raise RuntimeError("kernelpilot_b200 extension missing: run python -m kernelpilot_b200.build")
+    w = CONFIGS[args.workload]
+    inputs = w.inputs("cuda", seed=rk.rank)
+    in_bytes = sum(t.numel() * t.element_size() for t in inputs)
+    flush = in_bytes < 2 * L2_BYTES
+    step = make_step(w, inputs, rk)
+
+    with ClockSampler(physical_gpu_index(rk.local_rank)) as clocks:
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        total_ms, per = time_steps(step, args.steps, flush, rk)
+    ms = total_ms / args.steps
+    value = rate(w, ms) * rk.world
+    peak, peak_src = roofline_peak(w)
+    # dominant kernel: the op's own launches, timed per call on the op's stream
+    local_ms = statistics.mean(per)
+    achieved = work_per_call(w) / (local_ms / 1e3) / (1e9 if w.bound == "hbm" else 1e12)
+    roof = {"bound": w.bound, "achieved": round(achieved, 2), "peak": peak,
+            "unit": "GB/s" if w.bound == "hbm" else "TFLOP/s",
+            "frac": round(achieved / peak, 4), "traffic": profiled_traffic(w),
+            "peak_source": f"{peak_src} (MEASURED_PEAKS.json)" if peak_src == "measured"
+            else "fallback"}
+
+    e2e = time_e2e(w, inputs, args.e2e_steps, rk)
+
+    configs = {}
+    if rk.world == 1 and not args.no_configs:
+        del inputs, step
+        torch.cuda.empty_cache()
+        for key, other in CONFIGS.items():
+            if key == w.key:
+                continue
+            try:
+                configs[key] = quick_measure(other, rk)
+            except Exception as e:  # reported in the line, never hidden
+                configs[key] = {"error": f"{type(e).__name__}: {e}"[:300]}
+
+    cpu = None
+    if rk.world == 1 and rk.rank == 0 and not args.no_cpu:
+        cpu = time_cpu(w, reps=5)
+
+    if rk.world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rk.rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": unit_of(w), "n_gpus": rk.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": DTYPE_NAMES[w.dtype], "data": "synthetic",
+        "config": {"workload": w.key, "shape": list(w.shape), "description": w.description,
+                   "per_rank": "one full instance per GPU",
+                   "l2": "flushed between steps" if flush else "inputs larger than L2",
+                   "exchange": "all_reduce(SUM) of fp32 partials" if w.kernel == "reduce_sum"
+                   else "none", "parallelism": f"dp{rk.world}"},
+        "pct_of_peak": round(value * (1e3 if w.bound == "hbm" else 1.0) / (peak * rk.world), 4),
+        "roofline": roof,
+        "e2e": {k: (round(v, 5) if isinstance(v, float) else v) for k, v in e2e.items()},
+        "gpu_launches": LAUNCHES_PER_CALL[w.kernel] * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if cpu:
+        line["cpu_baseline"] = {k: (round(v, 5) if isinstance(v, float) else v)
+                                for k, v in cpu.items()}
+    if configs:
+        line["configs"] = configs
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,70 @@
+"""Host logic of the data-parallel layer with world_size 2 gloo ranks on CPU: shard
+ranges cover every unit once, the reduction partials combine into the global sum,
+and row blocks of unequal size assemble in rank order."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from kernelpilot_b200 import dist as kdist
+
+
+@pytest.mark.parametrize("n,world", [(0, 1), (1, 2), (7, 2), (10, 3), (2**28 + 1, 8)])
+def test_shard_ranges_partition(n, world):
+    spans = [kdist.shard_range(n, r, world) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == n
+    for (a0, b0), (a1, _b1) in zip(spans, spans[1:], strict=False):
+        assert b0 == a1
+    sizes = [b - a for a, b in spans]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_shard_range_rejects_bad_ranks():
+    with pytest.raises(ValueError):
+        kdist.shard_range(10, 2, 2)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    try:
+        kdist.init(backend="gloo", timeout_s=30)
+        g = torch.Generator().manual_seed(0)
+        x = torch.rand(1001, generator=g) * 2 - 1
+        a, b = kdist.shard_range(x.numel(), rank, world)
+        total = kdist.sharded_reduce_sum(x[a:b], lambda t: t.sum(dtype=torch.float32))
+        rows = torch.arange(7 * 3, dtype=torch.float32).reshape(7, 3)
+        ra, rb = kdist.shard_range(7, rank, world)
+        full = kdist.assemble_rows(torch.softmax(rows[ra:rb], -1),
+                                   kdist.row_counts(7, world))
+        q.put((rank, float(total), float(x.double().sum()),
+               bool(torch.allclose(full, torch.softmax(rows, -1)))))
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, "error", repr(e), False))
+
+
+def test_two_gloo_ranks_combine_partials_and_assemble_rows():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, total, want, assembled in results:
+        assert total != "error", want
+        assert abs(total - want) < 1e-3, (rank, total, want)
+        assert assembled

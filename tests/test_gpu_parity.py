@@ -1,0 +1,211 @@
+"""Parity of the sm_100a kernels with the float64 reference, on a GPU.
+
+* every registered implementation x dtype x spec test shape through ``check_impl``
+  (the reference's own gate, kernelpilot tests/gpu/test_correctness.py:17-31);
+* the reference's golden vectors (tests/golden, made from the reference package)
+  uploaded to the GPU, for every CUDA variant;
+* B200-specific edges: rows that do not start on a 16-byte boundary, rows longer
+  than one CTA holds, misaligned reduction inputs, GEMM shapes whose B rows are not
+  16-byte aligned, partial tiles;
+* the C ABI called directly with raw device pointers (ctypes);
+* determinism of the reduction, and no kernel wait ever timing out.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from kernelpilot_b200 import ext, registry
+from kernelpilot_b200.correctness import check_impl, check_on_inputs, compare
+from kernelpilot_b200.specs import SPECS, get_spec
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _cases():
+    for name, spec in SPECS.items():
+        for impl in ["torch"] + [f"cuda:{s}" for s in registry.CUDA_STAGES[name]]:
+            for dtype in spec.dtypes:
+                for shape in spec.test_shapes:
+                    yield pytest.param(name, impl, dtype, shape,
+                                       id=f"{name}-{impl}-{str(dtype)[6:]}-{shape}")
+
+
+def test_extension_built_and_in_tree():
+    assert ext.load(), "extension missing: run python -m kernelpilot_b200.build"
+    assert ext.library_path().parent == ext.LIB_DIR
+
+
+@pytest.mark.parametrize("kernel,impl,dtype,shape", list(_cases()))
+def test_kernel_matches_reference(kernel, impl, dtype, shape):
+    spec = SPECS[kernel]
+    fn = registry.get_impls(kernel)[impl]
+    res = check_impl(spec, impl, fn, shape, dtype, "cuda")
+    assert res.ok, res.summary()
+
+
+# ------------------------------------------------------------------ golden vectors
+
+def _golden(op):
+    blob = np.load(GOLDEN / f"{op}.npz")
+    keys = sorted({k.rsplit("|", 1)[0] for k in blob.files})
+    for key in keys:
+        dtype, shape_s = key.split("|")
+        shape = tuple(int(s) for s in shape_s.split(","))
+        n_in = sum(1 for k in blob.files if k.startswith(key + "|in"))
+        yield dtype, shape, [blob[f"{key}|in{i}"] for i in range(n_in)], blob[f"{key}|out"]
+
+
+def _to_device(a: np.ndarray, dtype: str) -> torch.Tensor:
+    if dtype == "bfloat16":
+        return torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16).cuda()
+    return torch.from_numpy(a.copy()).cuda()
+
+
+@pytest.mark.parametrize("op", list(SPECS))
+def test_golden_vectors_every_variant(op):
+    spec = get_spec(op)
+    for variant, stage in enumerate(registry.CUDA_STAGES[op]):
+        fn = registry.get_impls(op)[f"cuda:{stage}"]
+        for dtype, shape, ins, want in _golden(op):
+            xs = [_to_device(a, dtype) for a in ins]
+            out = fn(*xs)
+            torch.cuda.synchronize()
+            tol = spec.tolerance(shape, getattr(torch, dtype))
+            info = compare(out.cpu(), torch.from_numpy(want), tol.atol, tol.rtol)
+            assert info["num_mismatched"] == 0, (op, stage, dtype, shape, info)
+
+
+# ------------------------------------------------------------------ B200 edges
+
+EDGE = [
+    ("softmax", (33, 4097), torch.float32),      # rows start at 4-byte offsets
+    ("softmax", (7, 24577), torch.float32),      # just past the staged limit -> two-pass
+    ("softmax", (3, 100003), torch.float32),     # long misaligned rows, two-pass
+    ("softmax", (9, 32768), torch.bfloat16),     # staged, 4 vectors per thread
+    ("softmax", (5, 32769), torch.bfloat16),     # two-pass, misaligned
+    ("softmax", (300, 4095), torch.float16),     # odd rows, many CTAs per SM
+    ("softmax", (1500, 1), torch.float32),       # one element per row
+    ("reduce_sum", (2**24 + 3,), torch.float32),
+    ("reduce_sum", (5_000_011,), torch.bfloat16),
+    ("matmul", (4097, 264, 256), torch.bfloat16),
+    ("matmul", (300, 4097, 192), torch.bfloat16),  # B rows not 16-byte aligned
+    ("matmul", (129, 257, 72), torch.float16),
+    ("matmul", (512, 512, 4104), torch.bfloat16),
+    ("attention", (2, 3, 300, 128), torch.bfloat16),
+    ("attention", (1, 4, 513, 64), torch.float16),
+    ("attention_causal", (2, 3, 300, 128), torch.bfloat16),
+    ("attention_causal", (1, 2, 1000, 64), torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("kernel,shape,dtype", EDGE,
+                         ids=[f"{k}-{s}-{str(d)[6:]}" for k, s, d in EDGE])
+def test_edge_shapes_best_variant(kernel, shape, dtype):
+    res = check_impl(get_spec(kernel), "best", registry.best(kernel), shape, dtype, "cuda")
+    assert res.ok, res.summary()
+
+
+@pytest.mark.parametrize("offset", [1, 2, 3])
+def test_reduce_misaligned_input(offset):
+    spec = get_spec("reduce_sum")
+    base = spec.make_inputs((1_000_003,), torch.float32, torch.device("cuda"), 0)[0]
+    x = base[offset:]
+    assert x.data_ptr() % 16 != 0
+    res = check_on_inputs(spec, "best", registry.best("reduce_sum"), (x,), (x.numel(),),
+                          torch.float32)
+    assert res.ok, res.summary()
+
+
+@pytest.mark.parametrize("offset", [1, 3])
+def test_softmax_misaligned_base(offset):
+    spec = get_spec("softmax")
+    flat = spec.make_inputs((64 * 1000 + offset,), torch.float32, torch.device("cuda"), 0)[0]
+    x = flat[offset:].view(64, 1000)
+    res = check_on_inputs(spec, "best", registry.best("softmax"), (x,), (64, 1000),
+                          torch.float32)
+    assert res.ok, res.summary()
+
+
+def test_reduce_is_deterministic():
+    x = get_spec("reduce_sum").make_inputs((2**26 + 5,), torch.float32,
+                                           torch.device("cuda"), 3)[0]
+    fn = registry.best("reduce_sum")
+    a = fn(x)
+    b = fn(x)
+    assert torch.equal(a, b)
+
+
+def test_empty_inputs():
+    ops = ext.ops()
+    x = torch.empty(0, device="cuda")
+    assert float(ops.reduce_sum(x, 2)) == 0.0
+    assert ops.softmax(torch.empty(0, 5, device="cuda"), 2).shape == (0, 5)
+    a = torch.randn(3, 0, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(0, 4, device="cuda", dtype=torch.bfloat16)
+    assert torch.count_nonzero(ops.matmul(a, b, 3)) == 0
+
+
+def test_bad_inputs_raise():
+    ops = ext.ops()
+    with pytest.raises(RuntimeError, match="contiguous"):
+        ops.softmax(torch.randn(8, 8, device="cuda").t(), 2)
+    with pytest.raises(RuntimeError, match="variant"):
+        ops.softmax(torch.randn(8, 8, device="cuda"), 3)
+    with pytest.raises(RuntimeError, match="float32, float16 and bfloat16"):
+        ops.softmax(torch.randn(8, 8, device="cuda").double(), 2)
+    with pytest.raises(RuntimeError, match="same dtype"):
+        ops.matmul(torch.randn(8, 8, device="cuda"), torch.randn(8, 8, device="cuda").half(), 3)
+
+
+# ------------------------------------------------------------------ C ABI directly
+
+def _p(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+def test_capi_matches_torch_ops():
+    lib = ext.capi()
+    stream = ext.current_stream_ptr()
+    dev = torch.device("cuda")
+    ops = ext.ops()
+
+    x = get_spec("reduce_sum").make_inputs((3_000_001,), torch.float32, dev, 0)[0]
+    out = torch.empty((), device=dev)
+    ext.capi_check(lib.kpb_reduce_sum(2, 0, _p(x), _p(out), x.numel(), stream))
+    torch.cuda.synchronize()
+    assert torch.equal(out, ops.reduce_sum(x, 2))
+
+    x = get_spec("softmax").make_inputs((128, 4097), torch.bfloat16, dev, 0)[0]
+    y = torch.empty_like(x)
+    ext.capi_check(lib.kpb_softmax(2, 2, _p(x), _p(y), 128, 4097, stream))
+    torch.cuda.synchronize()
+    assert torch.equal(y, ops.softmax(x, 2))
+
+    a, b = get_spec("matmul").make_inputs((256, 300, 128), torch.bfloat16, dev, 0)
+    c = torch.empty(256, 300, dtype=torch.bfloat16, device=dev)
+    ext.capi_check(lib.kpb_matmul(3, 2, _p(a), _p(b), _p(c), 256, 300, 128, stream))
+    torch.cuda.synchronize()
+    assert torch.equal(c, ops.matmul(a, b, 3))
+
+    q, k, v = get_spec("attention").make_inputs((1, 2, 200, 128), torch.bfloat16, dev, 0)
+    o = torch.empty_like(q)
+    ext.capi_check(lib.kpb_attention(1, 2, _p(q), _p(k), _p(v), _p(o), 2, 200, 128, stream))
+    ext.capi_check(lib.kpb_attention_causal(1, 2, _p(q), _p(k), _p(v), _p(o), 2, 200, 128,
+                                            stream))
+    torch.cuda.synchronize()
+    assert torch.equal(o, ops.attention_causal(q, k, v, 1))
+
+
+def test_no_kernel_wait_timed_out():
+    lib = ext.capi()
+    bits = ctypes.c_uint(0)
+    ext.capi_check(lib.kpb_device_errors(ctypes.byref(bits)))
+    assert bits.value == 0
