@@ -217,11 +217,15 @@ softmax_staged(const T* __restrict__ x, T* __restrict__ y, int64_t M, int64_t N,
 
 // ------------------------------------------------------------------ variant 2: two-pass
 
-__device__ __forceinline__ void online_merge(float& m, float& d, float m2, float d2) {
-  const float mn = fmaxf(m, m2);
+// Online-softmax state: ml = round(max * log2e), d = sum of exp2(x*log2e - ml).
+// Every exponent is taken against a rounded ml with one FMA, and rescaling uses
+// differences of the same rounded values, so all partial sums stay consistent with
+// the final normalisation exp2(fma(x, log2e, -ml)).
+__device__ __forceinline__ void online_merge(float& ml, float& d, float ml2, float d2) {
+  const float mn = fmaxf(ml, ml2);
   if (mn == -INFINITY) return;
-  d = d * exp2f((m - mn) * kLog2e) + d2 * exp2f((m2 - mn) * kLog2e);
-  m = mn;
+  d = d * exp2f(ml - mn) + d2 * exp2f(ml2 - mn);
+  ml = mn;
 }
 
 template <typename T>
@@ -236,7 +240,7 @@ softmax_two_pass(const T* __restrict__ x, T* __restrict__ y, int64_t N) {
   const bool y_vec = ((reinterpret_cast<uintptr_t>(y) ^ reinterpret_cast<uintptr_t>(x)) & 15) == 0;
 
   // pass 1: online (max, sum); the row stays in L2 for pass 2 (normal priority)
-  float m = -INFINITY, d = 0.f;
+  float m = -INFINITY, d = 0.f;  // m holds round(max * log2e)
   for (int64_t j = threadIdx.x; j < rv.nv; j += blockDim.x) {
     const int64_t e0 = j * VN - rv.a;
     float f[VN];
@@ -250,12 +254,11 @@ softmax_two_pass(const T* __restrict__ x, T* __restrict__ y, int64_t N) {
     float vm = f[0];
 #pragma unroll
     for (int l = 1; l < VN; ++l) vm = fmaxf(vm, f[l]);
-    const float mn = fmaxf(m, vm);
-    const float mnl = mn * kLog2e;
+    const float mn = fmaxf(m, vm * kLog2e);
     float s = 0.f;
 #pragma unroll
-    for (int l = 0; l < VN; ++l) s += exp2f(fmaf(f[l], kLog2e, -mnl));
-    d = (m == -INFINITY ? 0.f : d * exp2f(fmaf(m, kLog2e, -mnl))) + s;
+    for (int l = 0; l < VN; ++l) s += exp2f(fmaf(f[l], kLog2e, -mn));
+    d = (m == -INFINITY ? 0.f : d * exp2f(m - mn)) + s;
     m = mn;
   }
 #pragma unroll
@@ -274,7 +277,7 @@ softmax_two_pass(const T* __restrict__ x, T* __restrict__ y, int64_t N) {
     const float m2 = __shfl_xor_sync(kFull, m, o), d2 = __shfl_xor_sync(kFull, d, o);
     online_merge(m, d, m2, d2);
   }
-  const float ml = m * kLog2e, inv = 1.f / d;
+  const float ml = m, inv = 1.f / d;
 
   // pass 2: normalise
   const uint64_t pol = evict_first_policy();
