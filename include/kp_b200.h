@@ -66,6 +66,18 @@ size_t kpb_reduce_sum_workspace_bytes(int variant, int64_t n);
 int kpb_reduce_sum_ws(int variant, int dtype, const void* x, float* out, int64_t n,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- full sum without allocation: no counterpart in the reference ----
+ * Same result as kpb_reduce_sum(2, ...) (the persistent kernel), for callers that may
+ * not allocate device memory when they call (a fixed start-up budget, memory owned by
+ * another allocator, no allocation after initialisation). The per-CTA partials live
+ * in a 16 KB array built into the library (held by every GPU that loads it until
+ * exit); calls needing more than 4096 partials are rejected with KPB_EINVAL. The
+ * first call on a device looks up the array's address: make it before any stream
+ * capture. All calls on a device share the array, so calls that overlap on the GPU
+ * race; order them on one stream. No cudaMalloc/cudaFree or allocating library call
+ * is made. */
+int kpb_reduce_sum_noalloc(int dtype, const void* x, float* out, int64_t n, void* stream);
+
 /* ---- row softmax: replaces kp::softmax (csrc/launchers.h:17-18) ----
  * y = softmax(x) over the last dimension of a contiguous (M, N) matrix;
  * fp32 math for every dtype; M, N < 2^31. */

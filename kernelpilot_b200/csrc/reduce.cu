@@ -175,6 +175,11 @@ int launch(int variant, const T* x, float* out, int64_t n, float* partials, cuda
 
 }  // namespace
 
+// Partials a call of `variant` on n elements writes on the current device.
+int64_t reduce_partials_needed(int variant, int64_t n) {
+  return n <= 0 ? 0 : level1_ctas(variant, n, sm_count());
+}
+
 size_t reduce_workspace_bytes(int variant, int64_t n) {
   if (n <= 0) return 0;
   // variant 2's CTA count depends on the SM count; size for the largest B200-class part

@@ -67,6 +67,7 @@ CAPI_SIGNATURES: dict[str, tuple] = {
     "kpb_reduce_sum": (_i32, [_i32, _i32, _vp, _vp, _i64, _vp]),
     "kpb_reduce_sum_workspace_bytes": (_sz, [_i32, _i64]),
     "kpb_reduce_sum_ws": (_i32, [_i32, _i32, _vp, _vp, _i64, _vp, _sz, _vp]),
+    "kpb_reduce_sum_noalloc": (_i32, [_i32, _vp, _vp, _i64, _vp]),
     "kpb_softmax": (_i32, [_i32, _i32, _vp, _vp, _i64, _i64, _vp]),
     "kpb_matmul": (_i32, [_i32, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "kpb_matmul_workspace_bytes": (_sz, [_i32, _i32, _i64, _i64, _i64]),
