@@ -18,10 +18,6 @@
 // Shapes TMA cannot describe (a row pitch that is not a multiple of 16 bytes, e.g.
 // N = 4097, or an unaligned base) are first copied into a zero-padded, aligned
 // workspace; C is written with masked stores, so any M, N, K works.
-#include <cudaTypedefs.h>
-
-#include <mutex>
-
 #include "kp_common.cuh"
 #include "kp_sm100.cuh"
 
@@ -217,39 +213,10 @@ __global__ void pad_cols(const T* __restrict__ src, T* __restrict__ dst, int64_t
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
-                                         &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 }  // namespace
 
-// Row-major (outer x inner) 16-bit matrix with a 128-byte-swizzled box of
-// (box_outer x 64); out-of-range elements read as zero.
 int make_tmap_2d_sw128(CUtensorMap* map, const void* base, bool bf16, uint64_t inner,
-                       uint64_t outer, uint64_t pitch_bytes, uint32_t box_outer) {
-  auto enc = tmap_encoder();
-  if (!enc) return fail(KPB_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {pitch_bytes};
-  cuuint32_t box[2] = {64, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                         2, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(KPB_ECUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
-  return KPB_OK;
-}
+                       uint64_t outer, uint64_t pitch_bytes, uint32_t box_outer);
 
 namespace {
 
