@@ -145,6 +145,23 @@ __device__ __forceinline__ void st_stream(void* p, const uint4& v) {
                :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
 }
 
+// ------------------------------------------------------------------ arithmetic
+
+// 2^x on the multi-function unit (ex2.approx.ftz: relative error about 2^-22; results
+// below 2^-126 flush to zero).
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // ------------------------------------------------------------------ warp / block reductions
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -33,7 +33,8 @@ constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreads = 192;
 constexpr int kGroupM = 16;
 constexpr uint32_t kTmemCols = 512;         // two 128 x 256 fp32 accumulators
-constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;  // + barriers + alignment
+constexpr int kEpiBytes = 4 * 32 * 17 * 4;  // epilogue transpose staging, 4 warps
+constexpr int kSmemBytes = kStages * kStageBytes + 256 + kEpiBytes + 1024;  // + barriers + alignment
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   const int group = kGroupM * num_n;
@@ -42,6 +43,17 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
   const int r = t % group;
   mb = first_m + r % rows;
   nb = r / rows;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2_t(float a, float b) {
+  if constexpr (std::is_same<T, __half>::value) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
 }
 
 template <typename T>
@@ -76,6 +88,7 @@ gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtenso
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint32_t* stage_out = reinterpret_cast<uint32_t*>(smem + kStages * kStageBytes + 256);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
@@ -186,7 +199,28 @@ gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtenso
         tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + c * 32, r);
         tmem_wait_ld();
         const int col0 = nb * BN + c * 32;
-        if (row < M && col0 < N) store_row32<T>(crow + col0, r, N - col0, vec_ok);
+        if (vec_ok) {
+          if (row < M && col0 < N) store_row32<T>(crow + col0, r, N - col0, true);
+        } else if (col0 < N) {
+          // C rows are not 16-byte aligned: transpose the warp's 32x32 chunk through
+          // shared memory so each store instruction writes 32 consecutive elements of
+          // one row (row stride 17 words: conflict-free in both directions)
+          uint32_t* st = stage_out + (warp - 2) * (32 * 17);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            st[lane * 17 + i] = pack2_t<T>(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+          __syncwarp();
+          const int64_t row0 = static_cast<int64_t>(mb) * BM + quarter * 32;
+          const bool col_ok = col0 + lane < N;
+#pragma unroll 4
+          for (int rr = 0; rr < 32; ++rr) {
+            const uint32_t w = st[rr * 17 + lane / 2];
+            const uint16_t h = static_cast<uint16_t>((lane & 1) ? (w >> 16) : (w & 0xFFFF));
+            if (col_ok && row0 + rr < M)
+              *reinterpret_cast<uint16_t*>(C + (row0 + rr) * ldc + col0 + lane) = h;
+          }
+          __syncwarp();
+        }
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -201,15 +235,27 @@ gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtenso
   }
 }
 
-// dst (rows x cols_pad) = src (rows x cols) with zero columns appended.
+// dst (rows x cols_pad) = src (rows x cols) with zero columns appended; cols_pad is a
+// multiple of 8, so every thread writes one aligned 16-byte vector of a dst row
+// (coalesced 2-byte reads of the unaligned source row).
 template <typename T>
 __global__ void pad_cols(const T* __restrict__ src, T* __restrict__ dst, int64_t rows,
                          int64_t cols, int64_t cols_pad) {
-  const int64_t total = rows * cols_pad;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = i / cols_pad, c = i % cols_pad;
-    dst[i] = c < cols ? src[r * cols + c] : from_f<T>(0.f);
+  const int64_t nvec = cols_pad / 8;
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const T* s = src + r * cols;
+    uint4* d = reinterpret_cast<uint4*>(dst + r * cols_pad);
+    for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
+         v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      uint16_t e[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int64_t c = v * 8 + i;
+        e[i] = c < cols ? reinterpret_cast<const uint16_t*>(s)[c] : uint16_t(0);
+      }
+      d[v] = make_uint4(e[0] | (uint32_t(e[1]) << 16), e[2] | (uint32_t(e[3]) << 16),
+                        e[4] | (uint32_t(e[5]) << 16), e[6] | (uint32_t(e[7]) << 16));
+    }
   }
 }
 
@@ -253,7 +299,7 @@ int launch_tc(const T* A, const T* B, T* C, int64_t M, int64_t N, int64_t K, voi
   const int sms = sm_count();
   if (st.pad_a) {
     T* ap = reinterpret_cast<T*>(w);
-    pad_cols<T><<<sms * 8, 256, 0, s>>>(A, ap, M, K, st.kp);
+    pad_cols<T><<<dim3(static_cast<unsigned>(cdiv(st.kp / 8, 256)), static_cast<unsigned>(std::min<int64_t>(M, 8192))), 256, 0, s>>>(A, ap, M, K, st.kp);
     KPB_LAUNCHED("matmul pad A");
     a = ap;
     lda = st.kp;
@@ -261,7 +307,7 @@ int launch_tc(const T* A, const T* B, T* C, int64_t M, int64_t N, int64_t K, voi
   }
   if (st.pad_b) {
     T* bp = reinterpret_cast<T*>(w);
-    pad_cols<T><<<sms * 8, 256, 0, s>>>(B, bp, K, N, st.np);
+    pad_cols<T><<<dim3(static_cast<unsigned>(cdiv(st.np / 8, 256)), static_cast<unsigned>(std::min<int64_t>(K, 8192))), 256, 0, s>>>(B, bp, K, N, st.np);
     KPB_LAUNCHED("matmul pad B");
     b = bp;
     ldb = st.np;
