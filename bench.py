@@ -10,8 +10,9 @@ scaling: the job is N instances); ops whose math needs an exchange step run it o
 NCCL inside the timed step (reduce_sum: all_reduce of the fp32 partials).
 
 value      whole-job algorithmic bytes (or FLOPs) / max-over-ranks device time,
-           inputs resident in HBM; per-step CUDA events, L2 flushed between steps
-           when the working set fits in L2 (the flush is outside the events).
+           inputs resident in HBM; per-step CUDA events; when the working set fits
+           in L2, L2 is flushed between steps outside the events (a 256 MB buffer
+           written, then read back so no dirty lines are left for the timed kernel).
 e2e        the same metric through the public API (torch.ops.kp) with the inputs
            copied from pinned host memory and the result copied back inside the
            timed region.
@@ -183,7 +184,7 @@ def time_steps(step, steps: int, flush: bool, rk: kdist.Rank) -> tuple[float, li
     torch.cuda.synchronize()
     for i in range(steps):
         if flush:
-            flush_l2()
+            flush_l2(clean=True)
         starts[i].record()
         step()
         ends[i].record()
@@ -412,7 +413,7 @@ def main() -> int:
         "dtype": DTYPE_NAMES[w.dtype], "data": "synthetic",
         "config": {"workload": w.key, "shape": list(w.shape), "description": w.description,
                    "per_rank": "one full instance per GPU",
-                   "l2": "flushed between steps" if flush else "inputs larger than L2",
+                   "l2": "flushed between steps outside the events (256 MB written, then read so no dirty lines remain)" if flush else "inputs larger than L2",
                    "exchange": "all_reduce(SUM) of fp32 partials" if w.kernel == "reduce_sum"
                    else "none", "parallelism": f"dp{rk.world}"},
         "pct_of_peak": round(value * (1e3 if w.bound == "hbm" else 1.0) / (peak * rk.world), 4),

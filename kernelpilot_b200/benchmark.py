@@ -28,11 +28,16 @@ L2_FLUSH_BYTES = 256 << 20  # larger than the 126 MB L2 of a B200
 _flush_buf: torch.Tensor | None = None
 
 
-def flush_l2() -> None:
+def flush_l2(clean: bool = False) -> None:
+    """Evict L2 by writing a 256 MB buffer (the reference harness's flush). With
+    ``clean`` the buffer is read back as well, so the dirty lines the write leaves
+    are written back here instead of during the next timed kernel."""
     global _flush_buf
     if _flush_buf is None:
         _flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     _flush_buf.zero_()
+    if clean:
+        _flush_buf.sum()
 
 
 def time_fn(fn: Callable, args: tuple, warmup: int = 10, iters: int = 100,

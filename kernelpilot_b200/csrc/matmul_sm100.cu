@@ -238,15 +238,42 @@ gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtenso
 // dst (rows x cols_pad) = src (rows x cols) with zero columns appended; cols_pad is a
 // multiple of 8, so every thread writes one aligned 16-byte vector of a dst row
 // (coalesced 2-byte reads of the unaligned source row).
+// Interior vectors read the two aligned 16-byte words that cover them and shift the
+// row's 2-byte misalignment out with funnel shifts; vectors at row or buffer ends
+// fall back to masked 2-byte loads.
+__device__ __forceinline__ uint32_t word_at(const uint4& a, const uint4& b, int i) {
+  switch (i) {
+    case 0: return a.x; case 1: return a.y; case 2: return a.z; case 3: return a.w;
+    case 4: return b.x; case 5: return b.y; case 6: return b.z; default: return b.w;
+  }
+}
+
 template <typename T>
 __global__ void pad_cols(const T* __restrict__ src, T* __restrict__ dst, int64_t rows,
                          int64_t cols, int64_t cols_pad) {
   const int64_t nvec = cols_pad / 8;
+  const uintptr_t src_lo = reinterpret_cast<uintptr_t>(src);
+  const uintptr_t src_hi = src_lo + static_cast<uintptr_t>(rows * cols) * 2;
   for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
     const T* s = src + r * cols;
     uint4* d = reinterpret_cast<uint4*>(dst + r * cols_pad);
+    const uintptr_t rs = reinterpret_cast<uintptr_t>(s);
+    const uintptr_t base = rs & ~uintptr_t(15);
+    const int off = static_cast<int>(rs - base);  // even, 0..14
     for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
          v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const uintptr_t w0 = base + static_cast<uintptr_t>(v) * 16;
+      if (v * 8 + 8 <= cols && w0 >= src_lo && w0 + 32 <= src_hi) {
+        const uint4 a = *reinterpret_cast<const uint4*>(w0);
+        const uint4 b = *reinterpret_cast<const uint4*>(w0 + 16);
+        const int q = off >> 2, sh = (off & 3) * 8;
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          o[i] = __funnelshift_r(word_at(a, b, q + i), word_at(a, b, q + i + 1), sh);
+        d[v] = make_uint4(o[0], o[1], o[2], o[3]);
+        continue;
+      }
       uint16_t e[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {

@@ -365,13 +365,16 @@ int64_t window_vectors(bool aligned, int64_t N) {
 template <typename T>
 StagedPlan plan_staged(int64_t nv_max) {
   StagedPlan p{};
+  // Cost of one row per CTA ~ threads * (V + 5): V vectors of element work plus a
+  // fixed per-row share (two block reductions, the slot wait, the refill) worth about
+  // five vectors. Fewer, fuller threads win for short rows.
   int64_t best = INT64_MAX;
-  for (int t = 128; t <= 1024; t += 128) {
+  for (int t = 64; t <= 1024; t += 64) {
     const int64_t v = cdiv(nv_max, t);
     if (v > staged_max_v<T>()) continue;
-    const int64_t slots = t * v;
-    if (slots < best || (slots == best && v < p.v)) {
-      best = slots;
+    const int64_t cost = t * (v + 5);
+    if (cost < best) {
+      best = cost;
       p.threads = t;
       p.v = static_cast<int>(v);
     }
