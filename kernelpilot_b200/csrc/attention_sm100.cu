@@ -27,7 +27,7 @@ namespace kpb {
 namespace {
 
 constexpr int BQ = 128, BKV = 128;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 softmax
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.f;  // log2 units: rescale O when max grows by > 256x
 
@@ -40,8 +40,9 @@ struct AttnSmem {
   static constexpr int kV = kK + 2 * kTile;        // 2 slots
   static constexpr int kPOff = kV + 2 * kTile;
   static constexpr int kPLoOff = kPOff + kP;       // rounding residual of P (few-key tiles)
-  static constexpr int kBar = kPLoOff + kP;
-  static constexpr int kBytes = kBar + 256 + 1024; // barriers + alignment slack
+  static constexpr int kRed = kPLoOff + kP;       // row max / sum exchange, 4 x 128 floats
+  static constexpr int kBar = kRed + 4 * 128 * 4;
+  static constexpr int kBytes = kBar + 256;        // + barriers (base is 1024-aligned)
 };
 
 // 16-byte chunk `c` (0..7) of row `r` in a 128-byte-swizzled tile of 128-byte rows.
@@ -75,6 +76,18 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Barrier over the 64 threads of a warp pair that also ANDs a predicate across them,
+// so both warps take every exit decision together.
+__device__ __forceinline__ bool pair_all(int id, bool p) {
+  uint32_t r;
+  asm volatile("{\n\t.reg .pred pi, po;\n\t"
+               "setp.ne.u32 pi, %1, 0;\n\t"
+               "bar.red.and.pred po, %2, 64, pi;\n\t"
+               "selp.u32 %0, 1, 0, po;\n\t}"
+               : "=r"(r) : "r"(static_cast<uint32_t>(p)), "r"(id) : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};"
@@ -90,9 +103,13 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
   constexpr int kAtoms = D / 64;              // 64-wide (128-byte) column atoms per row
   constexpr int kAtomBytes = BQ * 128;        // one atom column of a 128-row tile
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
+  // the 128-byte swizzle atoms need a 1024-byte aligned base; the layout leaves no
+  // room to realign, so report a misaligned base instead of computing garbage
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicOr(err, kErrSmemAlign);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
@@ -119,7 +136,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 11; ++i) mbar_init(&bars[i], 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(pv_done, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -223,44 +240,56 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
       mbar_wait(drain, 0, err);
     }
   } else {
-    // ------------------------------------------------ softmax + epilogue (warps 2..5)
+    // ------------------------------------------------ softmax + epilogue (warps 2..9)
+    // Two warps per TMEM lane quarter: warp w owns rows 32*(w%4) .. +31 and key
+    // columns [64*half, 64*half + 64) of each S tile, half = (w - 2) / 4. The pair
+    // shares the row max through shared memory behind a 64-thread named barrier.
     const int quarter = warp % 4;
+    const int half = (warp - 2) / 4;
     const int t = quarter * 32 + lane;          // query row within the tile (= TMEM lane)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t col_s = half * (BKV / 2);    // this warp's S / P columns
+    const uint32_t col_o = half * (D / 2);      // this warp's O columns
+    const int pair_bar = 1 + quarter;
     const int q = q0 + t;
-    const uint32_t p_hi = smem_u32(smem + L::kPOff);
-    const uint32_t p_lo = smem_u32(smem + L::kPLoOff);
+    const uint32_t p_hi = smem_u32(smem + L::kPOff) + half * kAtomBytes;
+    const uint32_t p_lo = smem_u32(smem + L::kPLoOff) + half * kAtomBytes;
+    float* red = reinterpret_cast<float*>(smem + L::kRed);  // [2 parities][2 halves][128 rows]
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int slot = j & 1;
-      ok = __all_sync(kFull, mbar_wait(&s_full[slot], (j >> 1) & 1, err));
-      if (!ok) break;
+      const bool s_ready = mbar_wait(&s_full[slot], (j >> 1) & 1, err);
       tc_fence_after();
       const int k0 = j * BKV;
-      // the whole S row in registers: one TMEM read
-      uint32_t r[BKV / 32][32];
-#pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) tmem_ld32(tmem + lane_base + slot * BKV + c * 32, r[c]);
+      uint32_t r[2][32];
+      tmem_ld32(tmem + lane_base + slot * BKV + col_s, r[0]);
+      tmem_ld32(tmem + lane_base + slot * BKV + col_s + 32, r[1]);
       tmem_wait_ld();
       // masking only on tiles that reach past S or cross the causal diagonal
       const bool edge = (k0 + BKV > S) || (kCausal && j == qt);
       if (edge) {
         int kend = min(S, k0 + BKV);
         if (kCausal) kend = min(kend, q + 1);
-        const int nvalid = kend - k0;
+        const int nvalid = kend - k0 - static_cast<int>(col_s);
 #pragma unroll
-        for (int c = 0; c < BKV / 32; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             if (c * 32 + i >= nvalid) r[c][i] = __float_as_uint(-INFINITY);
       }
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(r[c][i]));
-      const float mrow = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
+      for (int i = 0; i < 32; i += 2) {
+        mx0 = max3f(mx0, __uint_as_float(r[0][i]), __uint_as_float(r[0][i + 1]));
+        mx1 = max3f(mx1, __uint_as_float(r[1][i]), __uint_as_float(r[1][i + 1]));
+      }
+      float mx = fmaxf(mx0, mx1);
+      red[(slot * 2 + half) * BQ + t] = mx;
+      ok = pair_all(pair_bar, s_ready);
+      if (!ok) break;
+      mx = fmaxf(mx, red[(slot * 2 + (half ^ 1)) * BQ + t]);
+      const float mrow = mx * scale_log2;
       float corr = 1.f;
       bool rescale_o = false;
       if (mrow > m_used + kRescaleThreshold || (m_used == -INFINITY && mrow > -INFINITY)) {
@@ -270,43 +299,46 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
         m_used = mrow;
       }
       const float mneg = (m_used == -INFINITY) ? 0.f : -m_used;
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      const float2 sc2 = make_float2(scale_log2, scale_log2), mn2 = make_float2(mneg, mneg);
+      float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c)
+      for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float pv = ex2_approx(fmaf(__uint_as_float(r[c][i]), scale_log2, mneg));
-          r[c][i] = __float_as_uint(pv);
-          ls[i & 3] += pv;
+        for (int i = 0; i < 32; i += 2) {
+          float2 a = __ffma2_rn(make_float2(__uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1])),
+                                sc2, mn2);
+          a.x = ex2_approx(a.x);
+          a.y = ex2_approx(a.y);
+          r[c][i] = __float_as_uint(a.x);
+          r[c][i + 1] = __float_as_uint(a.y);
+          if (i & 2) ls1 = __fadd2_rn(ls1, a); else ls0 = __fadd2_rn(ls0, a);
         }
-      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      l += (ls0.x + ls0.y) + (ls1.x + ls1.y);
       // P buffers and O are free once PV_{j-1} completed
       if (j > 0) {
-        ok = __all_sync(kFull, mbar_wait(pv_done, (j - 1) & 1, err));
+        ok = pair_all(pair_bar, mbar_wait(pv_done, (j - 1) & 1, err));
         if (!ok) break;
         tc_fence_after();
       }
       if (__any_sync(kFull, rescale_o)) {
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < D / 64; ++c) {
           uint32_t o_r[32];
-          tmem_ld32(tmem_o + lane_base + c * 32, o_r);
+          tmem_ld32(tmem_o + lane_base + col_o + c * 32, o_r);
           tmem_wait_ld();
           const float f = rescale_o ? corr : 1.f;
 #pragma unroll
           for (int i = 0; i < 32; ++i) o_r[i] = __float_as_uint(__uint_as_float(o_r[i]) * f);
-          tmem_st32(tmem_o + lane_base + c * 32, o_r);
+          tmem_st32(tmem_o + lane_base + col_o + c * 32, o_r);
         }
         tmem_wait_st();
       }
-      // P (and, for tiles with few-key rows, the rounding residual P - P_hi) into
-      // 128-byte-swizzled K-major tiles: 32 keys = 4 chunks of 16 B in atom c / 2
+      // this warp's 64 keys fill one 128-byte swizzle atom of the P tile: 8 chunks
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        const uint32_t atom_off = (c / 2) * (BQ * 128);
+      for (int c = 0; c < 2; ++c) {
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
-          const int chunk = (c % 2) * 4 + h;
+          const int chunk = c * 4 + h;
           uint32_t w[4], wl[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -318,28 +350,33 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
               wl[e] = pack2<T>(a - hv.x, b - hv.y);
             }
           }
-          st_shared_v4(p_hi + atom_off + sw128(t, chunk), w[0], w[1], w[2], w[3]);
-          if (split) st_shared_v4(p_lo + atom_off + sw128(t, chunk), wl[0], wl[1], wl[2], wl[3]);
+          st_shared_v4(p_hi + sw128(t, chunk), w[0], w[1], w[2], w[3]);
+          if (split) st_shared_v4(p_lo + sw128(t, chunk), wl[0], wl[1], wl[2], wl[3]);
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    // epilogue: O / l -> global
-    if (ok && nkv > 0 && __all_sync(kFull, mbar_wait(pv_done, (nkv - 1) & 1, err))) {
+    // epilogue: O / l -> global; the row sum is the pair's two partial sums
+    if (ok && nkv > 0) {
+      red[((nkv & 1) * 2 + half) * BQ + t] = l;  // the parity buffer block nkv-1 did not use
+      ok = pair_all(pair_bar, mbar_wait(pv_done, (nkv - 1) & 1, err));
+      l += red[((nkv & 1) * 2 + (half ^ 1)) * BQ + t];
+    }
+    if (ok && nkv > 0) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* orow = o + (static_cast<int64_t>(bh) * S + q) * D;
+      T* orow = o + (static_cast<int64_t>(bh) * S + q) * D + col_o;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem_o + lane_base + c * 32, r);
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t rr[32];
+        tmem_ld32(tmem_o + lane_base + col_o + c * 32, rr);
         tmem_wait_ld();
         if (q < S) {
           float f[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(r[i]) * inv;
+          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(rr[i]) * inv;
 #pragma unroll
           for (int h = 0; h < 4; ++h)
             *reinterpret_cast<uint4*>(orow + c * 32 + 8 * h) = pack<T>(f + 8 * h);

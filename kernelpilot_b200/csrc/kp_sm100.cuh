@@ -15,6 +15,7 @@ constexpr uint64_t kWaitLimitNs = 4000000000ull;
 
 // Error bits a kernel may set in its error word.
 constexpr unsigned kErrTimeout = 1u;
+constexpr unsigned kErrSmemAlign = 2u;  // dynamic shared memory not 1024-byte aligned
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
