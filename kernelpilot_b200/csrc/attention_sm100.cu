@@ -76,6 +76,28 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// 2^x for two lanes on the FMA pipe: x = n + f with n = round(x) (added to 1.5*2^23 so
+// the rounded integer lands in the low mantissa bits), f in [-1/2, 1/2],
+// 2^f ~ c0 + f (c1 + f (c2 + f c3)) (coefficients from fit_exp2_poly.py: minimax
+// relative error 7.5e-5, far below the bf16/fp16 rounding P gets next), then n is
+// added to the exponent field. Inputs are <= 8 here; below -126 they clamp to
+// -126, so masked (-inf) scores give ~1e-38 rather than 0, which no output can see.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kMagic = 12582912.f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = __fadd2_rn(x, make_float2(kMagic, kMagic));
+  const float2 n = __fadd2_rn(t, make_float2(-kMagic, -kMagic));
+  const float2 f = __fadd2_rn(x, make_float2(-n.x, -n.y));
+  float2 p = __ffma2_rn(make_float2(0.0551716685295105f, 0.0551716685295105f), f,
+                        make_float2(0.2426111251115799f, 0.2426111251115799f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  p = __ffma2_rn(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  const int nx = __float_as_int(t.x) - 0x4B400000, ny = __float_as_int(t.y) - 0x4B400000;
+  return make_float2(__int_as_float(__float_as_int(p.x) + (nx << 23)),
+                     __int_as_float(__float_as_int(p.y) + (ny << 23)));
+}
+
 // Barrier over the 64 threads of a warp pair that also ANDs a predicate across them,
 // so both warps take every exit decision together.
 __device__ __forceinline__ bool pair_all(int id, bool p) {
@@ -307,8 +329,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
         for (int i = 0; i < 32; i += 2) {
           float2 a = __ffma2_rn(make_float2(__uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1])),
                                 sc2, mn2);
-          a.x = ex2_approx(a.x);
-          a.y = ex2_approx(a.y);
+          if ((i & 7) == 6) {
+            a = exp2_poly2(a);  // one pair in four on the FMA pipe: relieves the MUFU
+          } else {
+            a.x = ex2_approx(a.x);
+            a.y = ex2_approx(a.y);
+          }
           r[c][i] = __float_as_uint(a.x);
           r[c][i + 1] = __float_as_uint(a.y);
           if (i & 2) ls1 = __fadd2_rn(ls1, a); else ls0 = __fadd2_rn(ls0, a);
