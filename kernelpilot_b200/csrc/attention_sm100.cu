@@ -16,7 +16,7 @@
 //     over the first 64 columns of S_t as packed bf16/fp16 pairs and PV_t = P_t V_j
 //     reads it straight from TMEM (the A-from-TMEM form of tcgen05.mma), accumulating
 //     O_t in TMEM. While one tile's softmax runs, the tensor core works on the other;
-//   * warps 2-5 (tile A) and 6-9 (tile B): one thread per query row. The row's 128
+//   * warps 4-7 (tile A) and 8-11 (tile B): one thread per query row. The row's 128
 //     scores come from TMEM in one read; running max in log2 units; O is rescaled
 //     (TMEM load/scale/store of the row) only when the max grows by more than 2^8;
 //     three quarters of the exponentials run on the MUFU (ex2.approx) and one quarter
@@ -36,7 +36,11 @@ namespace {
 
 constexpr int BQ = 128, BKV = 128;
 constexpr int kTiles = 2;                   // query tiles per CTA
-constexpr int kThreads = 320;               // warp 0 TMA, 1 MMA, 2-5 tile A, 6-9 tile B
+constexpr int kThreads = 384;               // warpgroup 0: TMA, MMA, 2 idle; 1: tile A; 2: tile B
+// Register split (setmaxnreg): the launch gives 384 x 168; warpgroup 0 drops to 56 and
+// the two softmax warpgroups rise to 224: 128*56 + 256*224 = 384*168, and each
+// scheduler holds one warp of every warpgroup: (56 + 224 + 224) * 32 <= 16384.
+constexpr uint32_t kRegsProducer = 56, kRegsSoftmax = 224;
 constexpr uint32_t kTmemCols = 512;         // S_A | S_B | O_A | O_B, 128 columns each
 constexpr float kRescaleThreshold = 8.f;    // log2 units: rescale O when max grows > 256x
 
@@ -163,116 +167,119 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------ TMA loads
-      mbar_arrive_expect_tx(q_full, kTiles * L::kTile);
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(kRegsProducer));
+    if (warp == 0) {
+      if (lane == 0) {
+        // ------------------------------------------------ TMA loads
+        mbar_arrive_expect_tx(q_full, kTiles * L::kTile);
 #pragma unroll
-      for (int t = 0; t < kTiles; ++t)
+        for (int t = 0; t < kTiles; ++t)
 #pragma unroll
-        for (int a = 0; a < kAtoms; ++a)
-          tma_load_3d(smem + L::kQ + t * L::kTile + a * kAtomBytes, &tq, a * 64, q0 + t * BQ, bh,
-                      q_full);
-      bool ok = true;
-      for (int j = 0; j < nkv_max && ok; ++j) {
-        const int slot = j & 1;
-        const uint32_t ph = ((j >> 1) & 1) ^ 1;
-        if (!mbar_wait(&k_empty[slot], ph, err)) { ok = false; break; }
-        mbar_arrive_expect_tx(&k_full[slot], L::kTile);
+          for (int a = 0; a < kAtoms; ++a)
+            tma_load_3d(smem + L::kQ + t * L::kTile + a * kAtomBytes, &tq, a * 64, q0 + t * BQ, bh,
+                        q_full);
+        bool ok = true;
+        for (int j = 0; j < nkv_max && ok; ++j) {
+          const int slot = j & 1;
+          const uint32_t ph = ((j >> 1) & 1) ^ 1;
+          if (!mbar_wait(&k_empty[slot], ph, err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[slot], L::kTile);
 #pragma unroll
-        for (int a = 0; a < kAtoms; ++a)
-          tma_load_3d(smem + L::kK + slot * L::kTile + a * kAtomBytes, &tk, a * 64, j * BKV, bh,
-                      &k_full[slot]);
-        if (!mbar_wait(&v_empty[slot], ph, err)) { ok = false; break; }
-        mbar_arrive_expect_tx(&v_full[slot], L::kTile);
+          for (int a = 0; a < kAtoms; ++a)
+            tma_load_3d(smem + L::kK + slot * L::kTile + a * kAtomBytes, &tk, a * 64, j * BKV, bh,
+                        &k_full[slot]);
+          if (!mbar_wait(&v_empty[slot], ph, err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[slot], L::kTile);
 #pragma unroll
-        for (int a = 0; a < kAtoms; ++a)
-          tma_load_3d(smem + L::kV + slot * L::kTile + a * kAtomBytes, &tv, a * 64, j * BKV, bh,
-                      &v_full[slot]);
-      }
-      // drain: every issued copy has been consumed
-      if (ok) {
-        for (int j = max(0, nkv_max - 2); j < nkv_max; ++j) {
-          const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait(&k_empty[j & 1], ph, err)) break;
-          if (!mbar_wait(&v_empty[j & 1], ph, err)) break;
+          for (int a = 0; a < kAtoms; ++a)
+            tma_load_3d(smem + L::kV + slot * L::kTile + a * kAtomBytes, &tv, a * 64, j * BKV, bh,
+                        &v_full[slot]);
         }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------ MMA issue
-      constexpr uint32_t idesc_s = idesc_f16(BQ, BKV, kBf16, false, false);
-      constexpr uint32_t idesc_o = idesc_f16(BQ, D, kBf16, false, true);
-      const uint32_t q_addr = smem_u32(smem + L::kQ);
-      // K_j is last read by the S MMA of the last tile that still needs block j
-      auto k_last = [&](int t, int j) { return t == kTiles - 1 || j >= nkv1; };
-      auto issue_s = [&](int t, int j) {
-        const int slot = j & 1;
-        const uint32_t k_addr = smem_u32(smem + L::kK + slot * L::kTile);
-        const uint32_t qa = q_addr + t * L::kTile;
-#pragma unroll
-        for (int s = 0; s < D / 16; ++s) {
-          const uint32_t off = (s / 4) * kAtomBytes + (s % 4) * 32;
-          umma_f16_ss(tmem + t * BKV, smem_desc_sw128(qa + off, 16, 1024),
-                      smem_desc_sw128(k_addr + off, 16, 1024), idesc_s, s > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[t]);
-        if (k_last(t, j)) umma_commit(&k_empty[slot]);
-      };
-      auto issue_pv = [&](int t, int j) {
-        const int slot = j & 1;
-        const uint32_t v_addr = smem_u32(smem + L::kV + slot * L::kTile);
-        const uint32_t p_tmem = tmem + t * BKV;           // P_t: 64 packed columns
-        const uint32_t o_tmem = tmem + (kTiles + t) * BKV;
-#pragma unroll
-        for (int s = 0; s < BKV / 16; ++s)
-          umma_f16_ts(o_tmem, p_tmem + s * 8, smem_desc_sw128(v_addr + s * 16 * 128, kAtomBytes, 1024),
-                      idesc_o, (j > 0 || s > 0) ? 1u : 0u);
-        if (split) {
-#pragma unroll
-          for (int s = 0; s < BKV / 16; ++s)
-            umma_f16_ts(o_tmem, p_tmem + 64 + s * 8,
-                        smem_desc_sw128(v_addr + s * 16 * 128, kAtomBytes, 1024), idesc_o, 1u);
-        }
-        umma_commit(&pv_done[t]);
-        if (k_last(t, j)) umma_commit(&v_empty[slot]);
-      };
-      bool ok = mbar_wait(q_full, 0, err);
-      if (ok && nkv_max > 0) {
-        ok = mbar_wait(&k_full[0], 0, err);
-        tc_fence_after();
+        // drain: every issued copy has been consumed
         if (ok) {
-          for (int t = 0; t < kTiles; ++t)
-            if (nkv(t) > 0) issue_s(t, 0);
-        }
-      }
-      for (int j = 0; j < nkv_max && ok; ++j) {
-        const int slot = j & 1;
-        if (!mbar_wait(&v_full[slot], (j >> 1) & 1, err)) { ok = false; break; }
-        bool k_next_ready = false;
-        for (int t = 0; t < kTiles && ok; ++t) {
-          if (j >= nkv(t)) continue;
-          if (!mbar_wait(&p_full[t], j & 1, err)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(t, j);
-          if (j + 1 < nkv(t)) {
-            if (!k_next_ready) {
-              if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, err)) { ok = false; break; }
-              tc_fence_after();
-              k_next_ready = true;
-            }
-            issue_s(t, j + 1);
+          for (int j = max(0, nkv_max - 2); j < nkv_max; ++j) {
+            const uint32_t ph = (j >> 1) & 1;
+            if (!mbar_wait(&k_empty[j & 1], ph, err)) break;
+            if (!mbar_wait(&v_empty[j & 1], ph, err)) break;
           }
         }
       }
-      umma_commit(drain);
-      mbar_wait(drain, 0, err);
+    } else if (warp == 1) {
+      if (lane == 0) {
+        // ------------------------------------------------ MMA issue
+        constexpr uint32_t idesc_s = idesc_f16(BQ, BKV, kBf16, false, false);
+        constexpr uint32_t idesc_o = idesc_f16(BQ, D, kBf16, false, true);
+        const uint32_t q_addr = smem_u32(smem + L::kQ);
+        // K_j is last read by the S MMA of the last tile that still needs block j
+        auto k_last = [&](int t, int j) { return t == kTiles - 1 || j >= nkv1; };
+        auto issue_s = [&](int t, int j) {
+          const int slot = j & 1;
+          const uint32_t k_addr = smem_u32(smem + L::kK + slot * L::kTile);
+          const uint32_t qa = q_addr + t * L::kTile;
+#pragma unroll
+          for (int s = 0; s < D / 16; ++s) {
+            const uint32_t off = (s / 4) * kAtomBytes + (s % 4) * 32;
+            umma_f16_ss(tmem + t * BKV, smem_desc_sw128(qa + off, 16, 1024),
+                        smem_desc_sw128(k_addr + off, 16, 1024), idesc_s, s > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[t]);
+          if (k_last(t, j)) umma_commit(&k_empty[slot]);
+        };
+        auto issue_pv = [&](int t, int j) {
+          const int slot = j & 1;
+          const uint32_t v_addr = smem_u32(smem + L::kV + slot * L::kTile);
+          const uint32_t p_tmem = tmem + t * BKV;           // P_t: 64 packed columns
+          const uint32_t o_tmem = tmem + (kTiles + t) * BKV;
+#pragma unroll
+          for (int s = 0; s < BKV / 16; ++s)
+            umma_f16_ts(o_tmem, p_tmem + s * 8, smem_desc_sw128(v_addr + s * 16 * 128, kAtomBytes, 1024),
+                        idesc_o, (j > 0 || s > 0) ? 1u : 0u);
+          if (split) {
+#pragma unroll
+            for (int s = 0; s < BKV / 16; ++s)
+              umma_f16_ts(o_tmem, p_tmem + 64 + s * 8,
+                          smem_desc_sw128(v_addr + s * 16 * 128, kAtomBytes, 1024), idesc_o, 1u);
+          }
+          umma_commit(&pv_done[t]);
+          if (k_last(t, j)) umma_commit(&v_empty[slot]);
+        };
+        bool ok = mbar_wait(q_full, 0, err);
+        if (ok && nkv_max > 0) {
+          ok = mbar_wait(&k_full[0], 0, err);
+          tc_fence_after();
+          if (ok) {
+            for (int t = 0; t < kTiles; ++t)
+              if (nkv(t) > 0) issue_s(t, 0);
+          }
+        }
+        for (int j = 0; j < nkv_max && ok; ++j) {
+          const int slot = j & 1;
+          if (!mbar_wait(&v_full[slot], (j >> 1) & 1, err)) { ok = false; break; }
+          bool k_next_ready = false;
+          for (int t = 0; t < kTiles && ok; ++t) {
+            if (j >= nkv(t)) continue;
+            if (!mbar_wait(&p_full[t], j & 1, err)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(t, j);
+            if (j + 1 < nkv(t)) {
+              if (!k_next_ready) {
+                if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, err)) { ok = false; break; }
+                tc_fence_after();
+                k_next_ready = true;
+              }
+              issue_s(t, j + 1);
+            }
+          }
+        }
+        umma_commit(drain);
+        mbar_wait(drain, 0, err);
+      }
     }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(kRegsSoftmax));
     // ------------------------------------------------ softmax + epilogue
-    const int tile = (warp - 2) / 4;
+    const int tile = (warp - 4) / 4;
     const int quarter = warp % 4;
     const int row = quarter * 32 + lane;        // query row within the tile (= TMEM lane)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
