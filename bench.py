@@ -257,6 +257,14 @@ def reference_baseline(w: Workload):
     return w.spec.baseline, "reference"
 
 
+def subset_workload(w: Workload, n: int) -> Workload:
+    """The same workload with its leading dimension cut to n."""
+    import dataclasses
+
+    shape = (n,) + tuple(w.shape[1:])
+    return dataclasses.replace(w, key=f"{w.key}[subset {n}]", shape=shape)
+
+
 def cpu_sample(w: Workload) -> tuple[tuple, float, str]:
     """A bounded CPU sample of the workload: (inputs, fraction of one call, label)."""
     gen_cpu = torch.device("cpu")
@@ -346,6 +354,9 @@ def main() -> int:
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the device-side table of the other headline workloads")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--subset", type=int, default=0,
+                    help="run a smaller instance: this many rows (softmax), rows of A (matmul), "
+                         "batches (attention) or elements (reduce_sum); for profiling")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -361,6 +372,8 @@ def main() -> int:
     if not ext.load():
         raise RuntimeError("kernelpilot_b200 extension missing: run python -m kernelpilot_b200.build")
     w = CONFIGS[args.workload]
+    if args.subset:
+        w = subset_workload(w, args.subset)
     inputs = w.inputs("cuda", seed=rk.rank)
     in_bytes = sum(t.numel() * t.element_size() for t in inputs)
     flush = in_bytes < 2 * L2_BYTES
@@ -383,7 +396,7 @@ def main() -> int:
             "peak_source": f"{peak_src} (MEASURED_PEAKS.json)" if peak_src == "measured"
             else "fallback"}
 
-    e2e = time_e2e(w, inputs, args.e2e_steps, rk)
+    e2e = time_e2e(w, inputs, args.e2e_steps, rk) if args.e2e_steps > 0 else None
 
     configs = {}
     if rk.world == 1 and not args.no_configs:
@@ -418,7 +431,8 @@ def main() -> int:
                    else "none", "parallelism": f"dp{rk.world}"},
         "pct_of_peak": round(value * (1e3 if w.bound == "hbm" else 1.0) / (peak * rk.world), 4),
         "roofline": roof,
-        "e2e": {k: (round(v, 5) if isinstance(v, float) else v) for k, v in e2e.items()},
+        "e2e": ({k: (round(v, 5) if isinstance(v, float) else v) for k, v in e2e.items()}
+                if e2e else None),
         "gpu_launches": LAUNCHES_PER_CALL[w.kernel] * args.steps,
         "clocks": clocks.summary(),
     }
