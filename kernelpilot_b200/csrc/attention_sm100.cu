@@ -418,7 +418,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
 
 // (BH, S, D) 16-bit tensor as a 3-D TMA map with (64 x 128 x 1) boxes, 128-byte swizzle.
 int make_tmap_bhsd(CUtensorMap* map, const void* base, bool bf16, int64_t BH, int64_t S,
-                   int64_t D);
+                   int64_t D, uint32_t box_rows);
 
 namespace {
 
@@ -427,9 +427,9 @@ int launch_attn(const T* q, const T* k, const T* v, T* o, int64_t BH, int64_t S,
                 unsigned* err, cudaStream_t s) {
   constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mq, mk, mv;
-  if (int rc = make_tmap_bhsd(&mq, q, bf16, BH, S, D)) return rc;
-  if (int rc = make_tmap_bhsd(&mk, k, bf16, BH, S, D)) return rc;
-  if (int rc = make_tmap_bhsd(&mv, v, bf16, BH, S, D)) return rc;
+  if (int rc = make_tmap_bhsd(&mq, q, bf16, BH, S, D, 128)) return rc;
+  if (int rc = make_tmap_bhsd(&mk, k, bf16, BH, S, D, 128)) return rc;
+  if (int rc = make_tmap_bhsd(&mv, v, bf16, BH, S, D, 128)) return rc;
   auto kern = attn_fwd_tc<T, D, kCausal>;
   const int smem = AttnSmem<D>::kBytes;
   KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));

@@ -49,15 +49,15 @@ int make_tmap_2d_sw128(CUtensorMap* map, const void* base, bool bf16, uint64_t i
   return encode(map, bf16, 2, base, dims, strides, box);
 }
 
-// Contiguous (BH, S, D) 16-bit tensor as a 3-D map (D, S, BH) with (64 x 128 x 1)
+// Contiguous (BH, S, D) 16-bit tensor as a 3-D map (D, S, BH) with (64 x box_rows x 1)
 // boxes and 128-byte swizzle: rows past S of one head read as zero, never as the next
 // head's rows.
 int make_tmap_bhsd(CUtensorMap* map, const void* base, bool bf16, int64_t BH, int64_t S,
-                   int64_t D) {
+                   int64_t D, uint32_t box_rows) {
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S),
                               static_cast<cuuint64_t>(BH)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(S * D * 2)};
-  const cuuint32_t box[3] = {64, 128, 1};
+  const cuuint32_t box[3] = {64, box_rows, 1};
   return encode(map, bf16, 3, base, dims, strides, box);
 }
 
