@@ -10,8 +10,9 @@
 //   * warp 1 (one lane) issues tcgen05.mma (M=128, N=256, K=16) into one of two
 //     256-column fp32 accumulators in TMEM and releases ring slots / accumulators
 //     with tcgen05.commit;
-//   * warps 2-5 drain the other accumulator (tcgen05.ld -> bf16/fp16 -> global)
-//     while the next tile accumulates.
+//   * warps 2-9 drain the other accumulator (tcgen05.ld -> bf16/fp16 -> global)
+//     while the next tile accumulates; two warps share each 32-lane TMEM quarter
+//     and take alternate 32-column chunks.
 // Every mbarrier wait is bounded; a timeout sets the error word and the roles shut
 // down in order (wait for issued copies and MMAs, free TMEM, exit).
 //
@@ -30,10 +31,11 @@ constexpr int kABytes = BM * BK * 2;        // 16 KB
 constexpr int kBBoxBytes = BK * 64 * 2;     // one 64(K) x 64(N) box, 8 KB
 constexpr int kBBytes = BK * BN * 2;        // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + kEpiWarps * 32;
 constexpr int kGroupM = 16;
 constexpr uint32_t kTmemCols = 512;         // two 128 x 256 fp32 accumulators
-constexpr int kEpiBytes = 4 * 32 * 17 * 4;  // epilogue transpose staging, 4 warps
+constexpr int kEpiBytes = kEpiWarps * 32 * 17 * 4;  // epilogue transpose staging
 constexpr int kSmemBytes = kStages * kStageBytes + 256 + kEpiBytes + 1024;  // + barriers + alignment
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
@@ -102,7 +104,7 @@ gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtenso
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], kEpiWarps * 32);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -179,8 +181,10 @@ gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtenso
       mbar_wait(drain, 0, err);
     }
   } else {
-    // ---------------- epilogue: warps 2..5 cover TMEM lanes 32*(warp%4) ..
+    // ---------------- epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 and the
+    // 32-column chunks c = (w-2)/4, +2, +4, ...
     const int quarter = warp % 4;
+    const int chunk0 = (warp - 2) / 4;
     const int r_in_tile = quarter * 32 + lane;
     const bool vec_ok = (ldc % 8 == 0) && (reinterpret_cast<uintptr_t>(C) % 16 == 0);
     int acc = 0;
@@ -194,7 +198,7 @@ gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtenso
       const int64_t row = static_cast<int64_t>(mb) * BM + r_in_tile;
       T* crow = C + row * ldc;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = chunk0; c < BN / 32; c += 2) {
         uint32_t r[32];
         tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + c * 32, r);
         tmem_wait_ld();
@@ -303,8 +307,9 @@ Staging staging(const void* A, const void* B, int64_t M, int64_t N, int64_t K) {
   Staging s{};
   s.pad_a = (K % 8 != 0) || (reinterpret_cast<uintptr_t>(A) % 16 != 0);
   s.pad_b = (N % 8 != 0) || (reinterpret_cast<uintptr_t>(B) % 16 != 0);
-  s.kp = cdiv(K, 8) * 8;
-  s.np = cdiv(N, 8) * 8;
+  // staged pitches are whole 128-byte lines, so every 128-byte TMA box row is one line
+  s.kp = cdiv(K, 64) * 64;
+  s.np = cdiv(N, 64) * 64;
   s.a_bytes = s.pad_a ? static_cast<size_t>(cdiv(M * s.kp * 2, 256) * 256) : 0;
   s.b_bytes = s.pad_b ? static_cast<size_t>(cdiv(K * s.np * 2, 256) * 256) : 0;
   return s;
