@@ -19,8 +19,10 @@
 //   * warps 4-7 (tile A) and 8-11 (tile B): one thread per query row. The row's 128
 //     scores come from TMEM in one read; running max in log2 units; O is rescaled
 //     (TMEM load/scale/store of the row) only when the max grows by more than 2^8;
-//     three quarters of the exponentials run on the MUFU (ex2.approx) and one quarter
-//     on the FMA pipe (exp2_poly2); at the end O / l -> global.
+//     five eighths of the exponentials run on the MUFU (ex2.approx) and three eighths
+//     on the FMA pipe (exp2_poly2); P is packed and stored 32 keys at a time, and the
+//     row sum is taken after P has been handed to the tensor core (it is not on the
+//     S -> P -> PV -> S chain); at the end O / l -> global.
 // A tcgen05.commit tracks every MMA issued before it, so "S_t(j) is ready" also means
 // PV_t(j-1) has finished: the softmax never waits on the PV separately.
 // Masking: keys >= S, and keys > query on the causal diagonal tile, score -inf.
@@ -330,30 +332,25 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
       }
       const float mneg = (m_used == -INFINITY) ? 0.f : -m_used;
       const float2 sc2 = make_float2(scale_log2, scale_log2), mn2 = make_float2(mneg, mneg);
-      float2 ls[4];
+      // exponentials, 32 keys at a time, each chunk packed into P (over the first 64
+      // columns of S) as soon as it is done; for few-key rows also P - rounded P (next 64
+      // columns). The row sum waits until P has been handed to the tensor core.
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        ls[c] = make_float2(0.f, 0.f);
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           float2 a = __ffma2_rn(make_float2(__uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1])),
                                 sc2, mn2);
-          if ((i & 7) == 6) {
-            a = exp2_poly2(a);  // one pair in four on the FMA pipe: relieves the MUFU
+          const int pair = (i / 2) & 7;
+          if (pair == 1 || pair == 4 || pair == 6) {
+            a = exp2_poly2(a);  // three pairs in eight on the FMA pipe: relieves the MUFU
           } else {
             a.x = ex2_approx(a.x);
             a.y = ex2_approx(a.y);
           }
           r[c][i] = __float_as_uint(a.x);
           r[c][i + 1] = __float_as_uint(a.y);
-          ls[c] = __fadd2_rn(ls[c], a);
         }
-      }
-      l += ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y));
-      // P (and, for few-key rows, P - rounded P) over the first 64 (next 64) columns
-      // of S, 32 keys at a time so the packed words never coexist with all the scores
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e)
@@ -385,6 +382,16 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[tile]);
+      // row sum of this block's P, while the tensor core runs PV_t(j) and S_t(j+1)
+      float2 ls[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        ls[c] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2)
+          ls[c] = __fadd2_rn(ls[c], make_float2(__uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1])));
+      }
+      l += ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y));
     }
     // epilogue: O / l -> global
     if (ok && my_nkv > 0 && __all_sync(kFull, mbar_wait(&pv_done[tile], (my_nkv - 1) & 1, err))) {

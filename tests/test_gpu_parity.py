@@ -103,6 +103,12 @@ EDGE = [
     ("attention", (1, 4, 513, 64), torch.float16),
     ("attention_causal", (2, 3, 300, 128), torch.bfloat16),
     ("attention_causal", (1, 2, 1000, 64), torch.bfloat16),
+    # D = 128: a single query, ragged S (partial K/V and query tiles), and many heads
+    ("attention", (1, 1, 1, 128), torch.bfloat16),
+    ("attention", (1, 2, 129, 128), torch.float16),
+    ("attention", (3, 40, 384, 128), torch.bfloat16),
+    ("attention_causal", (1, 3, 257, 128), torch.float16),
+    ("attention_causal", (2, 40, 640, 128), torch.bfloat16),
 ]
 
 
