@@ -16,9 +16,11 @@
 //     over the first 64 columns of S_t as packed bf16/fp16 pairs and PV_t = P_t V_j
 //     reads it straight from TMEM (the A-from-TMEM form of tcgen05.mma), accumulating
 //     O_t in TMEM. While one tile's softmax runs, the tensor core works on the other;
-//   * warps 4-7 (tile A) and 8-11 (tile B): one thread per query row. The row's 128
-//     scores come from TMEM in one read; running max in log2 units; O is rescaled
-//     (TMEM load/scale/store of the row) only when the max grows by more than 2^8;
+//   * warps 4-11 (tile A) and 12-19 (tile B): two threads per query row, one per key
+//     half (64 of the block's 128 scores each, read from TMEM in one go); they swap
+//     their half-row maxima through shared memory (one 64-thread named barrier per
+//     block); running max in log2 units; O is rescaled (TMEM load/scale/store, half
+//     the columns each) only when the max grows by more than 2^8;
 //     five eighths of the exponentials run on the MUFU (ex2.approx) and three eighths
 //     on the FMA pipe (exp2_poly2); P is packed and stored 32 keys at a time, and the
 //     row sum is taken after P has been handed to the tensor core (it is not on the
@@ -38,11 +40,14 @@ namespace {
 
 constexpr int BQ = 128, BKV = 128;
 constexpr int kTiles = 2;                   // query tiles per CTA
-constexpr int kThreads = 384;               // warpgroup 0: TMA, MMA, 2 idle; 1: tile A; 2: tile B
-// Register split (setmaxnreg): the launch gives 384 x 168; warpgroup 0 drops to 56 and
-// the two softmax warpgroups rise to 224: 128*56 + 256*224 = 384*168, and each
-// scheduler holds one warp of every warpgroup: (56 + 224 + 224) * 32 <= 16384.
-constexpr uint32_t kRegsProducer = 56, kRegsSoftmax = 224;
+// warpgroup 0: TMA, MMA, 2 idle; warpgroups 1-2: tile A; 3-4: tile B. Each query row
+// is shared by two warps of its tile (keys 0..63 and 64..127 of every block), which
+// exchange only the block's row max.
+constexpr int kThreads = 640;
+// Register split (setmaxnreg): the launch gives 640 x 96; warpgroup 0 drops to 56 and
+// the four softmax warpgroups rise to 104: 128*56 + 512*104 = 60416 <= 640*96 = 61440,
+// and each scheduler holds one producer and four softmax warps: (56 + 4*104) * 32 <= 16384.
+constexpr uint32_t kRegsProducer = 56, kRegsSoftmax = 104;
 constexpr uint32_t kTmemCols = 512;         // S_A | S_B | O_A | O_B, 128 columns each
 constexpr float kRescaleThreshold = 8.f;    // log2 units: rescale O when max grows > 256x
 
@@ -53,7 +58,11 @@ struct AttnSmem {
   static constexpr int kK = kQ + kTiles * kTile;  // 2 slots
   static constexpr int kV = kK + 2 * kTile;       // 2 slots
   static constexpr int kBar = kV + 2 * kTile;
-  static constexpr int kBytes = kBar + 256;       // base is 1024-byte aligned
+  // row-max exchange between the two warps of a row: [block parity][tile][half][row]
+  // floats, then the same layout of ok flags, then the half-row sums for the epilogue
+  static constexpr int kX = kBar + 256;
+  static constexpr int kXMax = 0, kXOk = 2 * kTiles * 2 * BQ * 4, kXSum = 2 * kXOk;
+  static constexpr int kBytes = kX + kXSum + kTiles * 2 * BQ * 4;  // base is 1024-byte aligned
 };
 
 // 2^x on the multi-function unit (ex2.approx.ftz: max relative error ~2^-22).
@@ -105,11 +114,15 @@ __device__ __forceinline__ float2 unpack2(uint32_t w) {
     return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
 }
 
-template <typename T, int D, bool kCausal>
+// kSplit: the CTAs whose rows see only a handful of keys carry P as hi + lo (a separate
+// instantiation, launched on its own small grid: the extra live registers of the lo
+// part would otherwise spill in every CTA). A CTA's 256-query block is
+// ct_first + ct_step * blockIdx.x.
+template <typename T, int D, bool kCausal, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
             const __grid_constant__ CUtensorMap tv, T* __restrict__ o, int S, float scale_log2,
-            unsigned* err) {
+            int ct_first, int ct_step, unsigned* err) {
   using L = AttnSmem<D>;
   constexpr int kAtoms = D / 64;              // 64-wide (128-byte) column atoms per row
   constexpr int kAtomBytes = BQ * 128;        // one atom column of a 128-row tile
@@ -134,8 +147,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int n_ct = static_cast<int>(gridDim.x);
-  const int ct = kCausal ? n_ct - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
+  const int ct = ct_first + ct_step * static_cast<int>(blockIdx.x);
   const int bh = blockIdx.y;
   const int q0 = ct * kTiles * BQ;
   const int nkv_all = (S + BKV - 1) / BKV;
@@ -147,12 +159,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
   const int nkv0 = tile_nkv(0), nkv1 = tile_nkv(1);
   auto nkv = [&](int t) { return t == 0 ? nkv0 : nkv1; };
   const int nkv_max = max(nkv0, nkv1);
-  const bool split = (kCausal && ct == 0) || S <= 256;
+  constexpr bool split = kSplit;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 11; ++i) mbar_init(&bars[i], 1);
     for (int t = 0; t < kTiles; ++t) {
-      mbar_init(&p_full[t], 128);
+      mbar_init(&p_full[t], 256);  // every softmax thread of the tile
       mbar_init(&pv_done[t], 1);
     }
     mbar_init(drain, 1);
@@ -281,47 +293,68 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(kRegsSoftmax));
     // ------------------------------------------------ softmax + epilogue
-    const int tile = (warp - 4) / 4;
+    const int sw = warp - 4;                    // softmax warp 0..15
+    const int tile = sw / 8;
+    const int half = (sw / 4) & 1;              // keys 64*half .. 64*half+63 of every block
     const int quarter = warp % 4;
     const int row = quarter * 32 + lane;        // query row within the tile (= TMEM lane)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_tmem = tmem + lane_base + tile * BKV;
-    const uint32_t o_tmem = tmem + lane_base + (kTiles + tile) * BKV;
+    const uint32_t o_tmem = tmem + lane_base + (kTiles + tile) * BKV + half * (D / 2);
     const int qt = ct * kTiles + tile;
     const int q = q0 + tile * BQ + row;
     const int my_nkv = nkv(tile);
+    // exchange slots: this thread's and its partner's (same row, other key half)
+    float* xmax = reinterpret_cast<float*>(smem + L::kX + L::kXMax);
+    int* xok = reinterpret_cast<int*>(smem + L::kX + L::kXOk);
+    float* xsum = reinterpret_cast<float*>(smem + L::kX + L::kXSum);
+    const int x_me = (tile * 2 + half) * BQ + row, x_peer = (tile * 2 + 1 - half) * BQ + row;
+    constexpr int kXStride = kTiles * 2 * BQ;   // one block parity
+    // named barrier of the row's two warps; both always reach it together (the ok flags
+    // travel through the exchange, so a failed wait ends the loop in both warps at once)
+    const int bar_id = 1 + tile * 4 + quarter;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < my_nkv; ++j) {
-      ok = __all_sync(kFull, mbar_wait(&s_full[tile], j & 1, err));
+      const bool got = __all_sync(kFull, mbar_wait(&s_full[tile], j & 1, err));
+      const int k0 = j * BKV + half * 64;
+      uint32_t r[2][32];
+      float hmax = -INFINITY;
+      if (got) {
+        tc_fence_after();
+        tmem_ld32(s_tmem + half * 64, r[0]);
+        tmem_ld32(s_tmem + half * 64 + 32, r[1]);
+        tmem_wait_ld();
+        // masking only on blocks that reach past S or cross the causal diagonal
+        const bool edge = (j * BKV + BKV > S) || (kCausal && j == qt);
+        if (edge) {
+          int kend = S;
+          if (kCausal) kend = min(kend, q + 1);
+          const int nvalid = kend - k0;
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i >= nvalid) r[c][i] = __float_as_uint(-INFINITY);
+        }
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            mx[2 * c] = max3f(mx[2 * c], __uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1]));
+            mx[2 * c + 1] = max3f(mx[2 * c + 1], __uint_as_float(r[c][i + 2]), __uint_as_float(r[c][i + 3]));
+          }
+        hmax = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3]));
+      }
+      const int xb = (j & 1) * kXStride;
+      xmax[xb + x_me] = hmax;
+      xok[xb + x_me] = got ? 1 : 0;
+      asm volatile("bar.sync %0, 64;" :: "r"(bar_id) : "memory");
+      const float pmax = xmax[xb + x_peer];
+      ok = got && xok[xb + x_peer] != 0;
       if (!ok) break;
-      tc_fence_after();
-      const int k0 = j * BKV;
-      uint32_t r[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + c * 32, r[c]);
-      tmem_wait_ld();
-      // masking only on tiles that reach past S or cross the causal diagonal
-      const bool edge = (k0 + BKV > S) || (kCausal && j == qt);
-      if (edge) {
-        int kend = min(S, k0 + BKV);
-        if (kCausal) kend = min(kend, q + 1);
-        const int nvalid = kend - k0;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i >= nvalid) r[c][i] = __float_as_uint(-INFINITY);
-      }
-      float mx[4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        mx[c] = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < 32; i += 2)
-          mx[c] = max3f(mx[c], __uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1]));
-      }
-      const float mrow = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * scale_log2;
+      const float mrow = fmaxf(hmax, pmax) * scale_log2;
       float corr = 1.f;
       bool rescale_o = false;
       if (mrow > m_used + kRescaleThreshold || (m_used == -INFINITY && mrow > -INFINITY)) {
@@ -332,11 +365,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
       }
       const float mneg = (m_used == -INFINITY) ? 0.f : -m_used;
       const float2 sc2 = make_float2(scale_log2, scale_log2), mn2 = make_float2(mneg, mneg);
-      // exponentials, 32 keys at a time, each chunk packed into P (over the first 64
-      // columns of S) as soon as it is done; for few-key rows also P - rounded P (next 64
-      // columns). The row sum waits until P has been handed to the tensor core.
+      // exponentials, 32 keys at a time, each chunk packed into P as soon as it is done
+      // (this half's 64 keys: packed columns 32*half.. of S); for few-key rows also
+      // P - rounded P (columns 64 + 32*half..). The row sum waits until P has been
+      // handed to the tensor core.
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           float2 a = __ffma2_rn(make_float2(__uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1])),
@@ -355,7 +389,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
 #pragma unroll
         for (int e = 0; e < 16; ++e)
           w[e] = pack2<T>(__uint_as_float(r[c][2 * e]), __uint_as_float(r[c][2 * e + 1]));
-        tmem_st16(s_tmem + c * 16, w);
+        tmem_st16(s_tmem + half * 32 + c * 16, w);
         if (split) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
@@ -363,53 +397,63 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
             w[e] = pack2<T>(__uint_as_float(r[c][2 * e]) - hv.x,
                             __uint_as_float(r[c][2 * e + 1]) - hv.y);
           }
-          tmem_st16(s_tmem + 64 + c * 16, w);
+          tmem_st16(s_tmem + 64 + half * 32 + c * 16, w);
         }
       }
-      // PV_t(j-1) is complete (covered by the commit behind s_full), so O can be rescaled
+      // PV_t(j-1) is complete (covered by the commit behind s_full), so O can be
+      // rescaled; each of the row's two threads scales half of O's columns
       if (__any_sync(kFull, rescale_o)) {
+        // 16 columns at a time: the block's 64 P values stay live for the row sum
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
-          uint32_t o_r[32];
-          tmem_ld32(o_tmem + c * 32, o_r);
+          uint32_t o_r[16];
+          tmem_ld16(o_tmem + c * 16, o_r);
           tmem_wait_ld();
           const float f = rescale_o ? corr : 1.f;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o_r[i] = __float_as_uint(__uint_as_float(o_r[i]) * f);
-          tmem_st32(o_tmem + c * 32, o_r);
+          for (int i = 0; i < 16; ++i) o_r[i] = __float_as_uint(__uint_as_float(o_r[i]) * f);
+          tmem_st16(o_tmem + c * 16, o_r);
         }
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[tile]);
-      // row sum of this block's P, while the tensor core runs PV_t(j) and S_t(j+1)
-      float2 ls[4];
+      // this half's share of the row sum, while the tensor core runs PV_t(j) and S_t(j+1)
+      float2 ls[2];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         ls[c] = make_float2(0.f, 0.f);
 #pragma unroll
         for (int i = 0; i < 32; i += 2)
           ls[c] = __fadd2_rn(ls[c], make_float2(__uint_as_float(r[c][i]), __uint_as_float(r[c][i + 1])));
       }
-      l += ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y));
+      l += (ls[0].x + ls[0].y) + (ls[1].x + ls[1].y);
     }
-    // epilogue: O / l -> global
-    if (ok && my_nkv > 0 && __all_sync(kFull, mbar_wait(&pv_done[tile], (my_nkv - 1) & 1, err))) {
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* orow = o + (static_cast<int64_t>(bh) * S + q) * D;
+    // epilogue: both halves' sums -> O / l -> global, each thread half of the row
+    if (my_nkv > 0) {
+      const bool done =
+          ok && __all_sync(kFull, mbar_wait(&pv_done[tile], (my_nkv - 1) & 1, err));
+      xsum[x_me] = done ? l : -1.f;  // a sum is never negative: -1 = this half failed
+      asm volatile("bar.sync %0, 64;" :: "r"(bar_id) : "memory");
+      const float l_peer = xsum[x_peer];
+      if (done && l_peer >= 0.f) {
+        tc_fence_after();
+        const float lsum = l + l_peer;
+        const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+        T* orow = o + (static_cast<int64_t>(bh) * S + q) * D + half * (D / 2);
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(o_tmem + c * 32, rr);
-        tmem_wait_ld();
-        if (q < S) {
-          float f[32];
+        for (int c = 0; c < D / 64; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(o_tmem + c * 32, rr);
+          tmem_wait_ld();
+          if (q < S) {
+            float f[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(rr[i]) * inv;
+            for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(rr[i]) * inv;
 #pragma unroll
-          for (int h = 0; h < 4; ++h)
-            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * h) = pack<T>(f + 8 * h);
+            for (int h = 0; h < 4; ++h)
+              *reinterpret_cast<uint4*>(orow + c * 32 + 8 * h) = pack<T>(f + 8 * h);
+          }
         }
       }
     }
@@ -437,13 +481,27 @@ int launch_attn(const T* q, const T* k, const T* v, T* o, int64_t BH, int64_t S,
   if (int rc = make_tmap_bhsd(&mq, q, bf16, BH, S, D, 128)) return rc;
   if (int rc = make_tmap_bhsd(&mk, k, bf16, BH, S, D, 128)) return rc;
   if (int rc = make_tmap_bhsd(&mv, v, bf16, BH, S, D, 128)) return rc;
-  auto kern = attn_fwd_tc<T, D, kCausal>;
   const int smem = AttnSmem<D>::kBytes;
-  KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  const dim3 grid(static_cast<unsigned>(cdiv(S, kTiles * BQ)), static_cast<unsigned>(BH));
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
-  kern<<<grid, kThreads, smem, s>>>(mq, mk, mv, o, static_cast<int>(S), scale_log2, err);
-  KPB_LAUNCHED("attention tcgen05");
+  const int n_ct = static_cast<int>(cdiv(S, kTiles * BQ));
+  // few-key rows: every block when S <= 256, else the first causal block of each head
+  const int n_split = S <= kTiles * BQ ? n_ct : (kCausal ? 1 : 0);
+  if (n_ct > n_split) {
+    // causal: heaviest blocks first
+    auto kern = attn_fwd_tc<T, D, kCausal, false>;
+    KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const dim3 grid(static_cast<unsigned>(n_ct - n_split), static_cast<unsigned>(BH));
+    kern<<<grid, kThreads, smem, s>>>(mq, mk, mv, o, static_cast<int>(S), scale_log2,
+                                      kCausal ? n_ct - 1 : n_split, kCausal ? -1 : 1, err);
+    KPB_LAUNCHED("attention tcgen05");
+  }
+  if (n_split > 0) {
+    auto kern = attn_fwd_tc<T, D, kCausal, true>;
+    KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const dim3 grid(static_cast<unsigned>(n_split), static_cast<unsigned>(BH));
+    kern<<<grid, kThreads, smem, s>>>(mq, mk, mv, o, static_cast<int>(S), scale_log2, 0, 1, err);
+    KPB_LAUNCHED("attention tcgen05 few-key rows");
+  }
   return KPB_OK;
 }
 
