@@ -50,8 +50,17 @@ METRIC = json.loads((REPO / "BASELINE.json").read_text())["metric"] \
 DEFAULT_WORKLOAD = "reduce_f32_2p28p1"
 L2_BYTES = 126 * 1024 * 1024
 # kernel launches of ours per op call (the op's level-1 kernel + finish, or one kernel)
-LAUNCHES_PER_CALL = {"reduce_sum": 2, "softmax": 1, "matmul": 1, "attention": 1,
-                     "attention_causal": 1}
+def launches_per_call(w: Workload) -> int:
+    """Kernels of ours one call of the best variant launches on this workload."""
+    if w.kernel == "reduce_sum":
+        return 2  # persistent level + one-CTA finish
+    if w.kernel == "matmul":
+        M, N, K = w.shape
+        # tensor-core GEMM, plus a pitch-padding copy per operand TMA cannot describe
+        return 1 + int((K * 2) % 16 != 0) + int((N * 2) % 16 != 0)
+    if w.kernel == "attention_causal":
+        return 2 if w.shape[2] > 256 else 1  # main grid + the few-key-rows grid
+    return 1
 DTYPE_NAMES = {torch.float32: "f32", torch.float16: "f16", torch.bfloat16: "bf16"}
 
 
@@ -185,6 +194,10 @@ def time_steps(step, steps: int, flush: bool, rk: kdist.Rank) -> tuple[float, li
     for i in range(steps):
         if flush:
             flush_l2(clean=True)
+            # ~50 us of GPU-side idle work after the flush, outside the timed region, so
+            # the start event, the step and the end event are already queued when the GPU
+            # reaches them (a late host would otherwise be timed as an idle gap)
+            torch.cuda._sleep(100_000)
         starts[i].record()
         step()
         ends[i].record()
@@ -389,6 +402,8 @@ def main() -> int:
     peak, peak_src = roofline_peak(w)
     # dominant kernel: the op's own launches, timed per call on the op's stream
     local_ms = statistics.mean(per)
+    step_stats = {"mean": round(local_ms, 5), "median": round(statistics.median(per), 5),
+                  "min": round(min(per), 5), "max": round(max(per), 5)}
     achieved = work_per_call(w) / (local_ms / 1e3) / (1e9 if w.bound == "hbm" else 1e12)
     roof = {"bound": w.bound, "achieved": round(achieved, 2), "peak": peak,
             "unit": "GB/s" if w.bound == "hbm" else "TFLOP/s",
@@ -422,6 +437,7 @@ def main() -> int:
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": unit_of(w), "n_gpus": rk.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "step_ms": step_stats,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": DTYPE_NAMES[w.dtype], "data": "synthetic",
         "config": {"workload": w.key, "shape": list(w.shape), "description": w.description,
@@ -433,7 +449,7 @@ def main() -> int:
         "roofline": roof,
         "e2e": ({k: (round(v, 5) if isinstance(v, float) else v) for k, v in e2e.items()}
                 if e2e else None),
-        "gpu_launches": LAUNCHES_PER_CALL[w.kernel] * args.steps,
+        "gpu_launches": launches_per_call(w) * args.steps,
         "clocks": clocks.summary(),
     }
     if cpu:
