@@ -132,8 +132,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
   // room to realign, so report a misaligned base instead of computing garbage
   if (smem_u32(smem) & 1023) {
     if (threadIdx.x == 0) atomicOr(err, kErrSmemAlign);
+    if (kSplit) pdl_wait_primary();
     return;
   }
+  // the few-key grid that follows a causal main grid may start on SMs this grid no
+  // longer needs (its rows are disjoint; it waits for this grid before it completes)
+  if (!kSplit) pdl_launch_dependents();
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
@@ -463,6 +467,9 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  // launched as a programmatic dependent of the main grid: complete only after it, so
+  // work queued behind this grid on the stream sees the whole output
+  if (kSplit) pdl_wait_primary();
 }
 
 }  // namespace
@@ -498,8 +505,21 @@ int launch_attn(const T* q, const T* k, const T* v, T* o, int64_t BH, int64_t S,
   if (n_split > 0) {
     auto kern = attn_fwd_tc<T, D, kCausal, true>;
     KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const dim3 grid(static_cast<unsigned>(n_split), static_cast<unsigned>(BH));
-    kern<<<grid, kThreads, smem, s>>>(mq, mk, mv, o, static_cast<int>(S), scale_log2, 0, 1, err);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(n_split), static_cast<unsigned>(BH));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    // after a main grid: programmatic dependent launch, so these CTAs fill the SMs
+    // the main grid's last CTAs leave idle (without a main grid, griddepcontrol.wait
+    // returns at once)
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = n_ct > n_split ? 1 : 0;
+    KPB_CUDA(cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, o, static_cast<int>(S), scale_log2, 0, 1,
+                                err));
     KPB_LAUNCHED("attention tcgen05 few-key rows");
   }
   return KPB_OK;
