@@ -1,0 +1,45 @@
+"""Host-side pieces of bench.py (no GPU): launch counts claimed in the JSON line and the
+algorithmic work each headline workload is measured against."""
+import dataclasses
+
+import pytest
+
+import bench
+from kernelpilot_b200.specs import CONFIGS
+
+
+@pytest.mark.parametrize("key,expected", [
+    ("reduce_f32_2p28p1", 2),             # persistent level + one-CTA finish
+    ("softmax_f32_4096x4097", 1),
+    ("softmax_bf16_65536x32768", 1),
+    ("gemm_bf16_8192", 1),
+    ("gemm_bf16_4097x4097x4096", 2),      # B's 8194-byte rows take a pitch copy first
+    ("attn_bf16_b8h32s4096d128", 1),
+    ("attn_causal_bf16_b8h32s4096d128", 2),  # main grid + the few-key-rows grid
+])
+def test_launches_per_call(key, expected):
+    assert bench.launches_per_call(CONFIGS[key]) == expected
+
+
+def test_launches_per_call_short_causal_is_one_grid():
+    w = CONFIGS["attn_causal_bf16_b8h32s4096d128"]
+    short = dataclasses.replace(w, shape=(w.shape[0], w.shape[1], 256, w.shape[3]))
+    assert bench.launches_per_call(short) == 1
+
+
+def test_launches_per_call_gemm_pads_each_unaligned_operand():
+    w = CONFIGS["gemm_bf16_8192"]
+    assert bench.launches_per_call(dataclasses.replace(w, shape=(512, 512, 4100))) == 2
+    assert bench.launches_per_call(dataclasses.replace(w, shape=(512, 4100, 4100))) == 3
+
+
+def test_work_per_call_is_the_spec_formula():
+    # the figures the roofline fractions are computed from (kernelpilot/specs.py formulas)
+    assert bench.work_per_call(CONFIGS["softmax_f32_4096x4097"]) == 2 * 4096 * 4097 * 4
+    assert bench.work_per_call(CONFIGS["reduce_f32_2p28p1"]) == 4 * (2**28 + 1) + 4
+    assert bench.work_per_call(CONFIGS["gemm_bf16_8192"]) == pytest.approx(2 * 8192**3)
+    assert bench.work_per_call(CONFIGS["attn_bf16_b8h32s4096d128"]) == pytest.approx(
+        4 * 8 * 32 * 4096 * 4096 * 128)
+    # causal: the useful FLOPs (half the scores plus the diagonal)
+    assert bench.work_per_call(CONFIGS["attn_causal_bf16_b8h32s4096d128"]) == pytest.approx(
+        4 * 8 * 32 * 4096 * 4097 / 2 * 128)
