@@ -8,8 +8,8 @@
 //   * one CTA per (head, 256 queries) = two 128-query tiles A and B that share every
 //     K/V tile; causal CTAs run heaviest first;
 //   * warp 0 (one lane): TMA loads of Q_A, Q_B once and of K_j / V_j (128 keys x D,
-//     128-byte swizzle; 3-D tensor maps, so rows past S read as zeros) into two
-//     2-slot rings;
+//     128-byte swizzle; 3-D tensor maps, so rows past S read as zeros) into a 2-slot
+//     ring, K_j and V_j of a block under one barrier;
 //   * warp 1 (one lane): tcgen05.mma issue in the order
 //       S_A0 S_B0 | PV_A0 S_A1 PV_B0 S_B1 | PV_A1 S_A2 PV_B1 S_B2 | ...
 //     S_t = Q_t K_j^T lands in TMEM (128 fp32 columns per tile); P_t is written back
@@ -140,15 +140,15 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
   if (!kSplit) pdl_launch_dependents();
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [tile]
-  uint64_t* p_full = bars + 11;  // [tile]
-  uint64_t* pv_done = bars + 13; // [tile]
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  // K_j and V_j travel together: one barrier per ring slot for both (every wait of
+  // the MMA-issuing thread costs the tensor core a bubble, so it waits once per block)
+  uint64_t* kv_full = bars + 1;  // [2]
+  uint64_t* kv_empty = bars + 3; // [2]
+  uint64_t* s_full = bars + 5;   // [tile]
+  uint64_t* p_full = bars + 7;   // [tile]
+  uint64_t* pv_done = bars + 9;  // [tile]
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int ct = ct_first + ct_step * static_cast<int>(blockIdx.x);
@@ -166,7 +166,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
   constexpr bool split = kSplit;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 11; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 7; ++i) mbar_init(&bars[i], 1);  // q_full, kv_full, kv_empty, s_full
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(&p_full[t], 256);  // every softmax thread of the tile
       mbar_init(&pv_done[t], 1);
@@ -201,25 +201,22 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
         for (int j = 0; j < nkv_max && ok; ++j) {
           const int slot = j & 1;
           const uint32_t ph = ((j >> 1) & 1) ^ 1;
-          if (!mbar_wait(&k_empty[slot], ph, err)) { ok = false; break; }
-          mbar_arrive_expect_tx(&k_full[slot], L::kTile);
+          if (!mbar_wait(&kv_empty[slot], ph, err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[slot], 2 * L::kTile);
 #pragma unroll
           for (int a = 0; a < kAtoms; ++a)
             tma_load_3d(smem + L::kK + slot * L::kTile + a * kAtomBytes, &tk, a * 64, j * BKV, bh,
-                        &k_full[slot]);
-          if (!mbar_wait(&v_empty[slot], ph, err)) { ok = false; break; }
-          mbar_arrive_expect_tx(&v_full[slot], L::kTile);
+                        &kv_full[slot]);
 #pragma unroll
           for (int a = 0; a < kAtoms; ++a)
             tma_load_3d(smem + L::kV + slot * L::kTile + a * kAtomBytes, &tv, a * 64, j * BKV, bh,
-                        &v_full[slot]);
+                        &kv_full[slot]);
         }
         // drain: every issued copy has been consumed
         if (ok) {
           for (int j = max(0, nkv_max - 2); j < nkv_max; ++j) {
             const uint32_t ph = (j >> 1) & 1;
-            if (!mbar_wait(&k_empty[j & 1], ph, err)) break;
-            if (!mbar_wait(&v_empty[j & 1], ph, err)) break;
+            if (!mbar_wait(&kv_empty[j & 1], ph, err)) break;
           }
         }
       }
@@ -229,7 +226,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
         constexpr uint32_t idesc_s = idesc_f16(BQ, BKV, kBf16, false, false);
         constexpr uint32_t idesc_o = idesc_f16(BQ, D, kBf16, false, true);
         const uint32_t q_addr = smem_u32(smem + L::kQ);
-        // K_j is last read by the S MMA of the last tile that still needs block j
+        // K_j / V_j are last read by the MMAs of the last tile that still needs block j;
+        // the slot is released after that tile's PV (its S was issued before)
         auto k_last = [&](int t, int j) { return t == kTiles - 1 || j >= nkv1; };
         auto issue_s = [&](int t, int j) {
           const int slot = j & 1;
@@ -242,7 +240,6 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
                         smem_desc_sw128(k_addr + off, 16, 1024), idesc_s, s > 0 ? 1u : 0u);
           }
           umma_commit(&s_full[t]);
-          if (k_last(t, j)) umma_commit(&k_empty[slot]);
         };
         auto issue_pv = [&](int t, int j) {
           const int slot = j & 1;
@@ -260,11 +257,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
                           smem_desc_sw128(v_addr + s * 16 * 128, kAtomBytes, 1024), idesc_o, 1u);
           }
           umma_commit(&pv_done[t]);
-          if (k_last(t, j)) umma_commit(&v_empty[slot]);
+          if (k_last(t, j)) umma_commit(&kv_empty[slot]);
         };
         bool ok = mbar_wait(q_full, 0, err);
         if (ok && nkv_max > 0) {
-          ok = mbar_wait(&k_full[0], 0, err);
+          ok = mbar_wait(&kv_full[0], 0, err);
           tc_fence_after();
           if (ok) {
             for (int t = 0; t < kTiles; ++t)
@@ -272,8 +269,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
           }
         }
         for (int j = 0; j < nkv_max && ok; ++j) {
-          const int slot = j & 1;
-          if (!mbar_wait(&v_full[slot], (j >> 1) & 1, err)) { ok = false; break; }
+          // K_j / V_j were waited for before S(j) was issued
           bool k_next_ready = false;
           for (int t = 0; t < kTiles && ok; ++t) {
             if (j >= nkv(t)) continue;
@@ -282,7 +278,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
             issue_pv(t, j);
             if (j + 1 < nkv(t)) {
               if (!k_next_ready) {
-                if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, err)) { ok = false; break; }
+                if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, err)) { ok = false; break; }
                 tc_fence_after();
                 k_next_ready = true;
               }
