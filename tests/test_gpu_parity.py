@@ -99,6 +99,12 @@ EDGE = [
     ("matmul", (300, 4097, 192), torch.bfloat16),  # B rows not 16-byte aligned
     ("matmul", (129, 257, 72), torch.float16),
     ("matmul", (512, 512, 4104), torch.bfloat16),
+    # ragged M and N (N % 256 = 208), long K
+    ("matmul", (1000, 2000, 3000), torch.bfloat16),
+    # one-column and one-row edge tiles, B rows not 16-byte aligned, several tile waves
+    ("matmul", (2049, 4097, 2048), torch.bfloat16),
+    # ragged everything in fp16 (N % 256 = 76, K % 64 = 8)
+    ("matmul", (777, 1100, 5000), torch.float16),
     ("attention", (2, 3, 300, 128), torch.bfloat16),
     ("attention", (1, 4, 513, 64), torch.float16),
     ("attention_causal", (2, 3, 300, 128), torch.bfloat16),
