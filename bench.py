@@ -281,9 +281,9 @@ def subset_workload(w: Workload, n: int) -> Workload:
 def cpu_sample(w: Workload) -> tuple[tuple, float, str]:
     """A bounded CPU sample of the workload: (inputs, fraction of one call, label)."""
     gen_cpu = torch.device("cpu")
-    if w.kernel == "reduce_sum":
+    if w.kernel in ("reduce_sum", "vector_add"):
         return w.make_inputs(w.shape, w.dtype, gen_cpu, 0), 1.0, "the full instance"
-    if w.kernel == "softmax":
+    if w.kernel in ("softmax", "layernorm"):
         M, N = w.shape
         rows = min(M, max(1, (64 << 20) // (N * 4)))
         return w.make_inputs((rows, N), w.dtype, gen_cpu, 0), rows / M, f"{rows} of {M} rows"

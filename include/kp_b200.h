@@ -42,9 +42,9 @@ const char* kpb_last_error(void);
 /* ABI version (major*100 + minor). */
 int kpb_version(void);
 
-/* Number of variants of an op ("reduce_sum", "softmax", "matmul", "attention",
- * "attention_causal"), or -1 for an unknown name. Mirrors check_variant's counts
- * (csrc/bindings.cpp:30-33, :77, :111). */
+/* Number of variants of an op ("vector_add", "reduce_sum", "softmax", "matmul",
+ * "layernorm", "attention", "attention_causal"), or -1 for an unknown name. Mirrors
+ * check_variant's counts (csrc/bindings.cpp:30-33, :77, :111). */
 int kpb_num_variants(const char* op);
 
 /* Error bits that kernels on the current device recorded since the last call
@@ -52,6 +52,12 @@ int kpb_num_variants(const char* op);
  * the reference, whose kernels have no waits. Synchronous; for tests and health
  * checks, not hot paths. */
 int kpb_device_errors(unsigned* bits);
+
+/* ---- elementwise add: replaces kp::vector_add (csrc/launchers.h:12-13) ----
+ * c[i] = a[i] + b[i] for i < n, added in fp32 and rounded to the dtype. a, b, c must
+ * be element-aligned; the fast variant needs no further alignment. */
+int kpb_vector_add(int variant, int dtype, const void* a, const void* b, void* c, int64_t n,
+                   void* stream);
 
 /* ---- full sum: replaces kp::reduce_sum (csrc/launchers.h:14-15) ----
  * out[0] = sum of x[0..n) accumulated in fp32. Unlike the reference, `out` need not
@@ -95,6 +101,13 @@ size_t kpb_matmul_workspace_bytes(int variant, int dtype, int64_t M, int64_t N, 
 int kpb_matmul_ws(int variant, int dtype, const void* A, const void* B, void* C, int64_t M,
                   int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
                   void* stream);
+
+/* ---- LayerNorm: replaces kp::layernorm (csrc/launchers.h:25-27) ----
+ * y = (x - mean) / sqrt(var + eps) * w + b over the last dimension of a contiguous
+ * (M, N) matrix; w, b have N elements; biased variance; fp32 statistics for every
+ * dtype; M, N < 2^31. eps is used as given (the reference does not check it). */
+int kpb_layernorm(int variant, int dtype, const void* x, const void* w, const void* b, void* y,
+                  int64_t M, int64_t N, float eps, void* stream);
 
 /* ---- attention forward: replaces kp::attention (csrc/launchers.h:28-30) ----
  * o = softmax(q k^T / sqrt(D)) v on contiguous (BH, S, D) q, k, v, o;

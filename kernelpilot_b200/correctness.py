@@ -194,7 +194,8 @@ def check_chunked(spec: KernelSpec, impl_name: str, inputs: tuple, out: torch.Te
     """Per-element check of an already computed ``out`` against the float64
     reference, evaluated block by block along the leading axis the reference is
     independent over: rows for softmax, rows of C for matmul, (B, H) slices for
-    attention. For reduce_sum the reference is one float64 sum of the input."""
+    attention, element blocks for vector_add. For reduce_sum the reference is one
+    float64 sum of the input."""
     tol = spec.tolerance(shape, dtype)
     res = CheckResult(kernel=spec.name, impl=impl_name, shape=tuple(shape),
                       dtype=_dtype_name(dtype), ok=False, atol=tol.atol, rtol=tol.rtol)
@@ -218,6 +219,20 @@ def check_chunked(spec: KernelSpec, impl_name: str, inputs: tuple, out: torch.Te
         for s, e in _row_blocks(x2.shape[0], rows):
             info = compare(o2[s:e], spec.reference(x2[s:e]), tol.atol, tol.rtol)
             _merge(acc, info, (s,))
+    elif name == "vector_add":
+        a, b = (t.reshape(-1) for t in inputs)
+        o1 = out.reshape(-1)
+        for s, e in _row_blocks(a.numel(), elems_per_chunk):
+            _merge(acc, compare(o1[s:e], spec.reference(a[s:e], b[s:e]), tol.atol, tol.rtol),
+                   (s,))
+    elif name == "layernorm":
+        x, w, b = inputs
+        N = x.shape[-1]
+        x2, o2 = x.reshape(-1, N), out.reshape(-1, N)
+        rows = max(1, elems_per_chunk // max(N, 1))
+        for s, e in _row_blocks(x2.shape[0], rows):
+            _merge(acc, compare(o2[s:e], spec.reference(x2[s:e], w, b), tol.atol, tol.rtol),
+                   (s,))
     elif name == "matmul":
         a, b = inputs
         bd = b.double()

@@ -1,8 +1,9 @@
 // torch.ops.kp.* on top of the C ABI in include/kp_b200.h.
 //
 // Same operator schemas and checks as kernelpilot's csrc/bindings.cpp:118-134
-// (inputs on the GPU and contiguous :25-28, matching dtypes :38/:71/:106, size limits
-// :60/:73/:109, variant ranges :30-33/:77/:111, launch on the current stream :12-17,
+// (inputs on the GPU and contiguous :25-28, matching shapes/dtypes :38/:71/:88-90/:106,
+// size limits :60/:73/:93/:109, variant ranges :30-33/:77/:111, launch on the current
+// stream :12-17,
 // fresh outputs from the caching allocator). Additions: bf16 inputs (dtype_of,
 // :19-23, accepted float32/float16 only) and the attention_causal operator.
 // Errors surface as c10::Error (Python RuntimeError) carrying kpb_last_error().
@@ -55,6 +56,19 @@ at::Tensor scratch(const at::Tensor& like, size_t bytes) {
                    like.options().dtype(at::kByte));
 }
 
+at::Tensor vector_add(const at::Tensor& a, const at::Tensor& b, int64_t variant) {
+  check_input(a, "a");
+  check_input(b, "b");
+  TORCH_CHECK(a.sizes() == b.sizes() && a.scalar_type() == b.scalar_type(),
+              "a and b must match in shape and dtype");
+  const int v = static_cast<int>(check_variant("vector_add", variant));
+  auto c = at::empty_like(a);
+  check_rc(kpb_vector_add(v, dtype_of(a), a.data_ptr(), b.data_ptr(), c.data_ptr(), a.numel(),
+                          current_stream(a)),
+           "vector_add");
+  return c;
+}
+
 at::Tensor reduce_sum(const at::Tensor& x, int64_t variant) {
   check_input(x, "x");
   const int v = static_cast<int>(check_variant("reduce_sum", variant));
@@ -102,6 +116,26 @@ at::Tensor matmul(const at::Tensor& a, const at::Tensor& b, int64_t variant) {
   return c;
 }
 
+at::Tensor layernorm(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b, double eps,
+                     int64_t variant) {
+  check_input(x, "x");
+  check_input(w, "weight");
+  check_input(b, "bias");
+  TORCH_CHECK(x.dim() >= 1, "layernorm needs at least 1 dimension");
+  const int64_t N = x.size(-1);
+  TORCH_CHECK(w.numel() == N && b.numel() == N, "weight and bias must have size ", N);
+  TORCH_CHECK(w.scalar_type() == x.scalar_type() && b.scalar_type() == x.scalar_type(),
+              "x, weight and bias must share a dtype");
+  const int var = static_cast<int>(check_variant("layernorm", variant));
+  auto y = at::empty_like(x);
+  const int64_t M = N == 0 ? 0 : x.numel() / N;
+  TORCH_CHECK(M < (int64_t{1} << 31) && N < (int64_t{1} << 31), "layernorm shape too large");
+  check_rc(kpb_layernorm(var, dtype_of(x), x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(),
+                         M, N, static_cast<float>(eps), current_stream(x)),
+           "layernorm");
+  return y;
+}
+
 at::Tensor attention_impl(const char* op, const at::Tensor& q, const at::Tensor& k,
                           const at::Tensor& v, int64_t variant) {
   check_input(q, "q");
@@ -138,17 +172,21 @@ at::Tensor attention_causal(const at::Tensor& q, const at::Tensor& k, const at::
 }  // namespace
 
 TORCH_LIBRARY(kp, m) {
+  m.def("vector_add(Tensor a, Tensor b, int variant) -> Tensor");
   m.def("reduce_sum(Tensor x, int variant) -> Tensor");
   m.def("softmax(Tensor x, int variant) -> Tensor");
   m.def("matmul(Tensor a, Tensor b, int variant) -> Tensor");
+  m.def("layernorm(Tensor x, Tensor weight, Tensor bias, float eps, int variant) -> Tensor");
   m.def("attention(Tensor q, Tensor k, Tensor v, int variant) -> Tensor");
   m.def("attention_causal(Tensor q, Tensor k, Tensor v, int variant) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(kp, CUDA, m) {
+  m.impl("vector_add", &vector_add);
   m.impl("reduce_sum", &reduce_sum);
   m.impl("softmax", &softmax);
   m.impl("matmul", &matmul);
+  m.impl("layernorm", &layernorm);
   m.impl("attention", &attention);
   m.impl("attention_causal", &attention_causal);
 }

@@ -17,6 +17,10 @@ int softmax(int variant, int dtype, const void* x, void* y, int64_t M, int64_t N
 size_t matmul_workspace_bytes(int variant, int dtype, int64_t M, int64_t N, int64_t K);
 int matmul(int variant, int dtype, const void* A, const void* B, void* C, int64_t M, int64_t N,
            int64_t K, void* ws, size_t ws_bytes, unsigned* err, cudaStream_t s);
+int vector_add(int variant, int dtype, const void* a, const void* b, void* c, int64_t n,
+               cudaStream_t s);
+int layernorm(int variant, int dtype, const void* x, const void* w, const void* b, void* y,
+              int64_t M, int64_t N, float eps, cudaStream_t s);
 int attention(int variant, int dtype, bool causal, const void* q, const void* k, const void* v,
               void* o, int64_t BH, int64_t S, int64_t D, unsigned* err, cudaStream_t s);
 
@@ -101,7 +105,7 @@ int kpb_version(void) { return 100; }
 int kpb_num_variants(const char* op) {
   if (op == nullptr) return -1;
   const std::string s(op);
-  if (s == "reduce_sum" || s == "softmax") return 3;
+  if (s == "vector_add" || s == "reduce_sum" || s == "softmax" || s == "layernorm") return 3;
   if (s == "matmul") return 4;
   if (s == "attention" || s == "attention_causal") return 2;
   return -1;
@@ -114,6 +118,16 @@ int kpb_device_errors(unsigned* bits) {
   KPB_CUDA(cudaMemcpyToSymbol(g_device_error_word, &zero, sizeof(zero)));
   if (bits) *bits = v;
   return KPB_OK;
+}
+
+int kpb_vector_add(int variant, int dtype, const void* a, const void* b, void* c, int64_t n,
+                   void* stream) {
+  g_last_error.clear();
+  if (int rc = check_common("vector_add", variant, dtype)) return rc;
+  if (n < 0) return fail(KPB_EINVAL, "vector_add: n must be >= 0");
+  if (n > 0 && (a == nullptr || b == nullptr || c == nullptr))
+    return fail(KPB_EINVAL, "vector_add: null pointer");
+  return vector_add(variant, dtype, a, b, c, n, static_cast<cudaStream_t>(stream));
 }
 
 size_t kpb_reduce_sum_workspace_bytes(int variant, int64_t n) {
@@ -159,6 +173,17 @@ int kpb_softmax(int variant, int dtype, const void* x, void* y, int64_t M, int64
   unsigned* err = nullptr;
   if (int rc = device_error_word(&err)) return rc;
   return softmax(variant, dtype, x, y, M, N, err, static_cast<cudaStream_t>(stream));
+}
+
+int kpb_layernorm(int variant, int dtype, const void* x, const void* w, const void* b, void* y,
+                  int64_t M, int64_t N, float eps, void* stream) {
+  g_last_error.clear();
+  if (int rc = check_common("layernorm", variant, dtype)) return rc;
+  if (M < 0 || N < 0 || M >= (int64_t{1} << 31) || N >= (int64_t{1} << 31))
+    return fail(KPB_EINVAL, "layernorm: M and N must be in [0, 2^31)");
+  if (M * N > 0 && (x == nullptr || w == nullptr || b == nullptr || y == nullptr))
+    return fail(KPB_EINVAL, "layernorm: null pointer");
+  return layernorm(variant, dtype, x, w, b, y, M, N, eps, static_cast<cudaStream_t>(stream));
 }
 
 size_t kpb_matmul_workspace_bytes(int variant, int dtype, int64_t M, int64_t N, int64_t K) {

@@ -64,6 +64,7 @@ CAPI_SIGNATURES: dict[str, tuple] = {
     "kpb_version": (_i32, []),
     "kpb_num_variants": (_i32, [ctypes.c_char_p]),
     "kpb_device_errors": (_i32, [ctypes.POINTER(ctypes.c_uint)]),
+    "kpb_vector_add": (_i32, [_i32, _i32, _vp, _vp, _vp, _i64, _vp]),
     "kpb_reduce_sum": (_i32, [_i32, _i32, _vp, _vp, _i64, _vp]),
     "kpb_reduce_sum_workspace_bytes": (_sz, [_i32, _i64]),
     "kpb_reduce_sum_ws": (_i32, [_i32, _i32, _vp, _vp, _i64, _vp, _sz, _vp]),
@@ -72,6 +73,7 @@ CAPI_SIGNATURES: dict[str, tuple] = {
     "kpb_matmul": (_i32, [_i32, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "kpb_matmul_workspace_bytes": (_sz, [_i32, _i32, _i64, _i64, _i64]),
     "kpb_matmul_ws": (_i32, [_i32, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "kpb_layernorm": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
     "kpb_attention": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "kpb_attention_causal": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
 }

@@ -11,8 +11,12 @@ additions are all additive:
   tolerance branch, exactly as the reference lambdas would give it);
 * ``ATTENTION_CAUSAL``: the same attention with an upper-triangular mask; its
   ``flops`` counts only the useful (unmasked) half;
-* ``CONFIGS``: the five headline workloads with their own generators (U(-1,1) for
-  the reduction, N(0,1)/sqrt(K) for the GEMM) next to ``make_inputs``.
+* ``VECTOR_ADD`` and ``LAYERNORM`` (kernelpilot/specs.py:77-101, 214-250), the
+  reference's remaining ``kp`` ops, with the same additions;
+* ``CONFIGS``: the headline workloads (the five of the reference's benchmark table,
+  plus causal attention, the elementwise add and LayerNorm) with their own generators
+  (U(-1,1) for the reduction and the add, N(0,1)/sqrt(K) for the GEMM) next to
+  ``make_inputs``.
 """
 
 from __future__ import annotations
@@ -85,6 +89,38 @@ def randn(shape: Shape, dtype: torch.dtype, device, gen: torch.Generator,
 
 def _half_or(fp32: Tolerance, other: Tolerance):
     return lambda s, dt: fp32 if dt == torch.float32 else other
+
+
+# ------------------------------------------------------------------ vector add
+
+def vector_add_reference(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    return a.double() + b.double()
+
+
+def _vector_add_inputs(shape, dtype, device, seed):
+    g = generator(device, seed)
+    return randn(shape, dtype, device, g), randn(shape, dtype, device, g)
+
+
+VECTOR_ADD = KernelSpec(
+    name="vector_add",
+    description="Elementwise c = a + b over 1-D tensors.",
+    signature="def kernel_fn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor  # same dtype as a",
+    make_inputs=_vector_add_inputs,
+    reference=vector_add_reference,
+    baseline=torch.add,
+    test_shapes=[(1,), (7,), (1000,), (1024,), (65537,), (1 << 20,), (3_000_001,)],
+    bench_shapes=[(1 << 24,), (1 << 26,)],
+    dtypes=list(ALL_DTYPES),
+    flops=lambda s: float(s[0]),
+    bytes_moved=lambda s, dt: 3.0 * s[0] * element_size(dt),
+    # fp32 / fp16 as the reference (kernelpilot/specs.py:99-100); bf16 gets rtol 4e-3:
+    # one bf16 rounding of the sum is already up to 2^-9 relative, above the fp16 1e-3
+    tolerance=lambda s, dt: (Tolerance(1e-6, 1e-6) if dt == torch.float32 else
+                             Tolerance(1e-3, 4e-3) if dt == torch.bfloat16 else
+                             Tolerance(1e-3, 1e-3)),
+    shape_names=("n",),
+)
 
 
 # ------------------------------------------------------------------ reduction
@@ -267,8 +303,49 @@ ATTENTION_CAUSAL = KernelSpec(
 )
 
 
+# ------------------------------------------------------------------ layernorm
+
+LAYERNORM_EPS = 1e-5
+
+
+def layernorm_reference(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor
+                        ) -> torch.Tensor:
+    # eps = 1e-5, biased variance, normalized over the last dimension.
+    return F.layer_norm(x.double(), (x.shape[-1],), weight.double(), bias.double(), 1e-5)
+
+
+def _layernorm_inputs(shape, dtype, device, seed):
+    M, N = shape
+    g = generator(device, seed)
+    x = randn((M, N), dtype, device, g, scale=2.0)
+    w = (1.0 + 0.1 * torch.randn(N, generator=g, device=device)).to(dtype)
+    b = (0.1 * torch.randn(N, generator=g, device=device)).to(dtype)
+    return x, w, b
+
+
+LAYERNORM = KernelSpec(
+    name="layernorm",
+    description="LayerNorm over the last dimension of a contiguous (M, N) tensor with "
+                "elementwise affine weight and bias of shape (N,), eps=1e-5, biased variance. "
+                "Output has the input dtype; compute statistics in float32.",
+    signature="def kernel_fn(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor)"
+              " -> torch.Tensor",
+    make_inputs=_layernorm_inputs,
+    reference=layernorm_reference,
+    baseline=lambda x, w, b: F.layer_norm(x, (x.shape[-1],), w, b, LAYERNORM_EPS),
+    test_shapes=[(1, 1), (1, 7), (3, 1000), (64, 1024), (17, 4097), (32, 12288), (2, 20000)],
+    bench_shapes=[(4096, 1024), (4096, 4096), (8192, 8192)],
+    dtypes=list(ALL_DTYPES),
+    flops=lambda s: 8.0 * s[0] * s[1],
+    bytes_moved=lambda s, dt: float((2 * s[0] * s[1] + 2 * s[1]) * element_size(dt)),
+    tolerance=_half_or(Tolerance(1e-5, 1e-4), Tolerance(5e-3, 1e-2)),
+    shape_names=("M", "N"),
+)
+
+
 SPECS: dict[str, KernelSpec] = {
-    s.name: s for s in [REDUCE_SUM, SOFTMAX, MATMUL, ATTENTION, ATTENTION_CAUSAL]
+    s.name: s for s in [VECTOR_ADD, REDUCE_SUM, SOFTMAX, MATMUL, LAYERNORM, ATTENTION,
+                        ATTENTION_CAUSAL]
 }
 
 
@@ -284,6 +361,12 @@ def _uniform_pm1(shape, dtype, device, seed):
     g = generator(device, seed)
     x = torch.rand(shape, generator=g, device=device, dtype=torch.float32) * 2.0 - 1.0
     return (x.to(dtype),)
+
+
+def _uniform_pm1_pair(shape, dtype, device, seed):
+    g = generator(device, seed)
+    return tuple((torch.rand(shape, generator=g, device=device, dtype=torch.float32) * 2.0 - 1.0)
+                 .to(dtype) for _ in range(2))
 
 
 def _matmul_scaled(shape, dtype, device, seed):
@@ -323,6 +406,12 @@ CONFIGS: dict[str, Workload] = {w.key: w for w in [
              _matmul_scaled, "tensor", "GEMM bf16 8192^3, N(0,1)/sqrt(K)"),
     Workload("gemm_bf16_4097x4097x4096", "matmul", (4097, 4097, 4096), torch.bfloat16,
              _matmul_scaled, "tensor", "GEMM bf16 M=N=4097 K=4096, N(0,1)/sqrt(K)"),
+    Workload("vadd_f32_2p26", "vector_add", (1 << 26,), torch.float32,
+             _uniform_pm1_pair, "hbm", "elementwise add fp32, n = 2^26, U(-1,1)"),
+    Workload("layernorm_f32_8192x8192", "layernorm", (8192, 8192), torch.float32,
+             _layernorm_inputs, "hbm", "LayerNorm fp32 [8192, 8192], x ~ N(0,1)*2, eps 1e-5"),
+    Workload("layernorm_bf16_8192x8192", "layernorm", (8192, 8192), torch.bfloat16,
+             _layernorm_inputs, "hbm", "LayerNorm bf16 [8192, 8192], x ~ N(0,1)*2, eps 1e-5"),
     Workload("attn_bf16_b8h32s4096d128", "attention", (8, 32, 4096, 128), torch.bfloat16,
              _attention_inputs, "tensor", "attention bf16 B8 H32 S4096 D128, non-causal"),
     Workload("attn_causal_bf16_b8h32s4096d128", "attention_causal", (8, 32, 4096, 128),

@@ -48,6 +48,22 @@ def as_f64(a: np.ndarray, dtype: str) -> np.ndarray:
 
 # ------------------------------------------------------------------ op semantics
 
+def vector_add(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """a.double() + b.double() (kernelpilot/specs.py:77-78)."""
+    return np.asarray(a, dtype=np.float64) + np.asarray(b, dtype=np.float64)
+
+
+def layernorm(x: np.ndarray, w: np.ndarray, b: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """F.layer_norm(x.double(), (N,), w, b, 1e-5) (kernelpilot/specs.py:217-220): per
+    row, subtract the mean, divide by sqrt(biased variance + eps), then scale by w and
+    shift by b."""
+    x = np.asarray(x, dtype=np.float64)
+    mean = np.mean(x, axis=-1, keepdims=True)
+    var = np.mean((x - mean) ** 2, axis=-1, keepdims=True)
+    return (x - mean) / np.sqrt(var + eps) * np.asarray(w, dtype=np.float64) + \
+        np.asarray(b, dtype=np.float64)
+
+
 def reduce_sum(x: np.ndarray) -> np.float64:
     """x.double().sum() (kernelpilot/specs.py:106-107), as a float64 scalar."""
     return np.float64(np.sum(np.asarray(x, dtype=np.float64)))
@@ -82,9 +98,13 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool = False)
 # ------------------------------------------------------------------ tolerances
 
 def tolerance(op: str, shape: tuple[int, ...], dtype: str) -> tuple[float, float]:
-    """(atol, rtol) per op and dtype (kernelpilot/specs.py:114-117, 165-166,
-    183-190, 281-282); bf16 takes the non-fp32 branch like fp16."""
+    """(atol, rtol) per op and dtype (kernelpilot/specs.py:99-100, 114-117, 165-166,
+    183-190, 246-247, 281-282); bf16 takes the non-fp32 branch like fp16."""
     fp32 = dtype == "float32"
+    if op == "vector_add":  # bf16: one rounding of the sum is up to 2^-9 relative
+        return (1e-6, 1e-6) if fp32 else ((1e-3, 4e-3) if dtype == "bfloat16" else (1e-3, 1e-3))
+    if op == "layernorm":
+        return (1e-5, 1e-4) if fp32 else (5e-3, 1e-2)
     if op == "reduce_sum":
         return 1e-5 * math.sqrt(shape[0]) + 1e-5, 1e-5
     if op == "softmax":
@@ -126,6 +146,10 @@ def compare(out: np.ndarray, ref: np.ndarray, atol: float, rtol: float) -> dict:
 def run(op: str, inputs: list[np.ndarray], dtype: str) -> np.ndarray:
     """The float64 reference output of ``op`` on (possibly bf16-bit) inputs."""
     xs = [as_f64(a, dtype) for a in inputs]
+    if op == "vector_add":
+        return vector_add(*xs)
+    if op == "layernorm":
+        return layernorm(*xs)
     if op == "reduce_sum":
         return np.asarray(reduce_sum(xs[0]))
     if op == "softmax":

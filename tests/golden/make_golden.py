@@ -3,7 +3,7 @@
 Run once, in a checkout that has the reference package available (its path is the
 first argument, default /root/reference):
 
-    python tests/golden/make_golden.py [/path/to/kernelpilot]
+    python tests/golden/make_golden.py [/path/to/kernelpilot] [op ...]
 
 For every op, dtype and shape below it calls the reference's own input generator
 (``spec.make_inputs(shape, dtype, cpu, seed=0)``, kernelpilot/specs.py:69-72) and its
@@ -28,9 +28,11 @@ import torch.nn.functional as F
 HERE = Path(__file__).resolve().parent
 
 SHAPES = {
+    "vector_add": [(1,), (7,), (1000,), (1024,), (65537,)],
     "reduce_sum": [(1,), (7,), (1000,), (1024,), (65537,)],
     "softmax": [(1, 1), (1, 7), (3, 1000), (17, 1024), (5, 4097), (2, 129)],
     "matmul": [(1, 1, 1), (7, 13, 5), (64, 64, 64), (127, 129, 65), (33, 100, 77)],
+    "layernorm": [(1, 1), (1, 7), (3, 1000), (17, 1024), (5, 4097), (2, 129)],
     "attention": [(1, 1, 1, 16), (1, 2, 7, 32), (1, 2, 64, 64), (1, 2, 100, 64),
                   (1, 3, 50, 48), (1, 1, 40, 128)],
 }
@@ -45,12 +47,14 @@ def to_np(t: torch.Tensor) -> np.ndarray:
     return t.numpy()
 
 
-def main(ref_root: str) -> None:
+def main(ref_root: str, ops: list[str]) -> None:
     sys.path.insert(0, ref_root)
     from kernelpilot.specs import get_spec  # the reference's own contract
 
     cpu = torch.device("cpu")
     for op, shapes in SHAPES.items():
+        if ops and op not in ops:
+            continue
         spec = get_spec("attention" if op == "attention_causal" else op)
         blob: dict[str, np.ndarray] = {}
         for dtype in DTYPES:
@@ -71,4 +75,4 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2:])

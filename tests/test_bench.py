@@ -16,6 +16,9 @@ from kernelpilot_b200.specs import CONFIGS
     ("gemm_bf16_4097x4097x4096", 2),      # B's 8194-byte rows take a pitch copy first
     ("attn_bf16_b8h32s4096d128", 1),
     ("attn_causal_bf16_b8h32s4096d128", 2),  # main grid + the few-key-rows grid
+    ("vadd_f32_2p26", 1),
+    ("layernorm_f32_8192x8192", 1),
+    ("layernorm_bf16_8192x8192", 1),
 ])
 def test_launches_per_call(key, expected):
     assert bench.launches_per_call(CONFIGS[key]) == expected
@@ -40,6 +43,9 @@ def test_work_per_call_is_the_spec_formula():
     assert bench.work_per_call(CONFIGS["gemm_bf16_8192"]) == pytest.approx(2 * 8192**3)
     assert bench.work_per_call(CONFIGS["attn_bf16_b8h32s4096d128"]) == pytest.approx(
         4 * 8 * 32 * 4096 * 4096 * 128)
+    assert bench.work_per_call(CONFIGS["vadd_f32_2p26"]) == 3 * 4 * 2**26
+    assert bench.work_per_call(CONFIGS["layernorm_bf16_8192x8192"]) == (
+        2 * 8192 * 8192 + 2 * 8192) * 2
     # causal: the useful FLOPs (half the scores plus the diagonal)
     assert bench.work_per_call(CONFIGS["attn_causal_bf16_b8h32s4096d128"]) == pytest.approx(
         4 * 8 * 32 * 4096 * 4097 / 2 * 128)

@@ -43,7 +43,9 @@ def test_version_and_variant_counts(lib):
     assert lib.kpb_num_variants(b"matmul") == 4
     assert lib.kpb_num_variants(b"attention") == 2
     assert lib.kpb_num_variants(b"attention_causal") == 2
-    assert lib.kpb_num_variants(b"layernorm") == -1
+    assert lib.kpb_num_variants(b"vector_add") == 3
+    assert lib.kpb_num_variants(b"layernorm") == 3
+    assert lib.kpb_num_variants(b"rmsnorm") == -1
 
 
 def test_variant_counts_match_registry(lib):
@@ -58,6 +60,13 @@ def test_variant_counts_match_registry(lib):
     (lambda L: L.kpb_softmax(2, 0, None, None, -1, 4, None), "M and N"),
     (lambda L: L.kpb_softmax(2, 0, None, None, 4, 4, None), "null"),
     (lambda L: L.kpb_reduce_sum(0, 0, None, None, 5, None), "null"),
+    (lambda L: L.kpb_vector_add(3, 0, None, None, None, 5, None), "variant"),
+    (lambda L: L.kpb_vector_add(2, 0, None, None, None, -1, None), "n must be"),
+    (lambda L: L.kpb_vector_add(2, 0, None, None, None, 5, None), "null"),
+    (lambda L: L.kpb_layernorm(3, 0, None, None, None, None, 4, 4, 1e-5, None), "variant"),
+    (lambda L: L.kpb_layernorm(2, 5, None, None, None, None, 4, 4, 1e-5, None), "dtype"),
+    (lambda L: L.kpb_layernorm(2, 0, None, None, None, None, 4, 1 << 31, 1e-5, None), "M and N"),
+    (lambda L: L.kpb_layernorm(2, 0, None, None, None, None, 4, 4, 1e-5, None), "null"),
     (lambda L: L.kpb_matmul_ws(4, 2, None, None, None, 2, 2, 2, None, 0, None), "variant"),
     (lambda L: L.kpb_matmul_ws(3, 2, None, None, None, 1 << 31, 2, 2, None, 0, None), "2^31"),
     (lambda L: L.kpb_attention(1, 2, None, None, None, None, 1, 8, 300, None), "D <= 256"),
@@ -78,8 +87,8 @@ def test_workspace_queries(lib):
 
 
 def test_ctypes_types_are_plain():
-    # the boundary has no torch types: every argument is an int, a size or a pointer
-    allowed = {ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p,
+    # the boundary has no torch types: every argument is an int, a float, a size or a pointer
+    allowed = {ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_float,
                ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint)}
     for _name, (_res, args) in ext.CAPI_SIGNATURES.items():
         assert all(a in allowed for a in args)

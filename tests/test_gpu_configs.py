@@ -1,8 +1,8 @@
 """Parity at the headline workloads' full sizes: the B200 kernel on each
 configuration's own seeded generator, checked element by element against the float64
 reference (evaluated in row / head blocks so the reference fits in memory), plus the
-size-independent properties each op has (softmax rows sum to one, the reduction is
-linear in its input)."""
+size-independent properties each op has (softmax rows sum to one, LayerNorm rows
+are standardised before the affine step, the reduction is linear in its input)."""
 
 from __future__ import annotations
 
@@ -28,6 +28,13 @@ def test_headline_workload_full_size(key):
         rows = out.float().sum(-1)
         tol = 1e-4 if w.dtype == torch.float32 else 2e-2
         assert float((rows - 1).abs().max()) < tol
+    if w.kernel == "layernorm":
+        # (y - b) / w has zero mean and unit (biased) variance in every row
+        x, wt, bs = inputs
+        z = (out.double() - bs.double()) / wt.double()
+        tol = 1e-4 if w.dtype == torch.float32 else 5e-2
+        assert float(z.mean(-1).abs().max()) < tol
+        assert float((z.var(-1, unbiased=False) - 1).abs().max()) < 2 * tol
     del inputs, out
     torch.cuda.empty_cache()
 

@@ -93,6 +93,18 @@ EDGE = [
     ("softmax", (5, 32769), torch.bfloat16),     # two-pass, misaligned
     ("softmax", (300, 4095), torch.float16),     # odd rows, many CTAs per SM
     ("softmax", (1500, 1), torch.float32),       # one element per row
+    ("layernorm", (33, 4097), torch.float32),    # rows at 4-byte offsets -> block per row
+    ("layernorm", (7, 32768), torch.float32),    # longest fp32 row held in registers
+    ("layernorm", (3, 32772), torch.float32),    # one vector past it -> block per row
+    ("layernorm", (9, 32768), torch.bfloat16),   # 16 warps x 8 vectors per row
+    ("layernorm", (5, 65536), torch.bfloat16),   # 32 warps x 8 vectors per row
+    ("layernorm", (5, 32769), torch.bfloat16),   # block per row, misaligned
+    ("layernorm", (300, 4095), torch.float16),   # odd rows
+    ("layernorm", (1500, 1), torch.float32),     # one element per row: y = b
+    ("layernorm", (1000, 8), torch.bfloat16),    # one vector per row, 8 rows per warp group
+    ("layernorm", (4096, 4096), torch.bfloat16), # two rows per CTA
+    ("vector_add", (2**24 + 3,), torch.float32),
+    ("vector_add", (5_000_011,), torch.bfloat16),
     ("reduce_sum", (2**24 + 3,), torch.float32),
     ("reduce_sum", (5_000_011,), torch.bfloat16),
     ("matmul", (4097, 264, 256), torch.bfloat16),
@@ -146,6 +158,46 @@ def test_softmax_misaligned_base(offset):
     assert res.ok, res.summary()
 
 
+@pytest.mark.parametrize("offsets", [(1, 1, 1), (1, 2, 3), (0, 0, 5), (3, 0, 0)])
+def test_vector_add_misaligned(offsets):
+    # equal offsets share a vector grid (scalar head + vector body); unequal ones do not
+    spec = get_spec("vector_add")
+    n = 1_000_003
+    a0, b0 = spec.make_inputs((n + 8,), torch.float16, torch.device("cuda"), 0)
+    a, b = a0[offsets[0]:offsets[0] + n], b0[offsets[1]:offsets[1] + n]
+    c0 = torch.empty(n + 8, dtype=torch.float16, device="cuda")
+    c = c0[offsets[2]:offsets[2] + n]
+    ext.capi_check(ext.capi().kpb_vector_add(2, 1, a.data_ptr(), b.data_ptr(), c.data_ptr(), n,
+                                             ext.current_stream_ptr()))
+    torch.cuda.synchronize()
+    assert torch.equal(c, (a.float() + b.float()).half())
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("x_off,p_off", [(1, 1), (3, 3), (0, 1), (1, 0), (1, 2), (0, 3)])
+def test_layernorm_misaligned_base_and_params(x_off, p_off, dtype):
+    # rows, w and b each at their own offset from a 16-byte boundary: the rows-in-
+    # registers kernel reads w/b as shifted pairs of aligned vectors
+    spec = get_spec("layernorm")
+    dev = torch.device("cuda")
+    M, N = 64, 1000
+    x0, w0, b0 = spec.make_inputs((M, N + 8), dtype, dev, 0)
+    x = x0.flatten()[x_off:x_off + M * N].view(M, N)
+    w, b = w0[p_off:p_off + N], b0[p_off:p_off + N]
+    res = check_on_inputs(spec, "best", registry.best("layernorm"), (x, w, b), (M, N), dtype)
+    assert res.ok, res.summary()
+
+
+def test_layernorm_constant_rows_give_bias():
+    # zero variance: (x - mean) is exactly 0, so y = b for any weight
+    ops = ext.ops()
+    x = torch.full((40, 3000), 7.25, device="cuda")
+    w = torch.randn(3000, device="cuda")
+    b = torch.randn(3000, device="cuda")
+    for v in range(3):
+        assert torch.equal(ops.layernorm(x, w, b, 1e-5, v), b.expand(40, 3000))
+
+
 def test_reduce_is_deterministic():
     x = get_spec("reduce_sum").make_inputs((2**26 + 5,), torch.float32,
                                            torch.device("cuda"), 3)[0]
@@ -163,6 +215,10 @@ def test_empty_inputs():
     a = torch.randn(3, 0, device="cuda", dtype=torch.bfloat16)
     b = torch.randn(0, 4, device="cuda", dtype=torch.bfloat16)
     assert torch.count_nonzero(ops.matmul(a, b, 3)) == 0
+    assert ops.vector_add(x, x, 2).shape == (0,)
+    e = torch.empty(0, 5, device="cuda")
+    assert ops.layernorm(e, torch.ones(5, device="cuda"), torch.zeros(5, device="cuda"),
+                         1e-5, 2).shape == (0, 5)
 
 
 def test_bad_inputs_raise():
@@ -173,6 +229,14 @@ def test_bad_inputs_raise():
         ops.softmax(torch.randn(8, 8, device="cuda"), 3)
     with pytest.raises(RuntimeError, match="float32, float16 and bfloat16"):
         ops.softmax(torch.randn(8, 8, device="cuda").double(), 2)
+    with pytest.raises(RuntimeError, match="match in shape"):
+        ops.vector_add(torch.randn(8, device="cuda"), torch.randn(9, device="cuda"), 2)
+    with pytest.raises(RuntimeError, match="must have size"):
+        ops.layernorm(torch.randn(4, 8, device="cuda"), torch.ones(7, device="cuda"),
+                      torch.zeros(8, device="cuda"), 1e-5, 2)
+    with pytest.raises(RuntimeError, match="share a dtype"):
+        ops.layernorm(torch.randn(4, 8, device="cuda"), torch.ones(8, device="cuda").half(),
+                      torch.zeros(8, device="cuda"), 1e-5, 2)
     with pytest.raises(RuntimeError, match="same dtype"):
         ops.matmul(torch.randn(8, 8, device="cuda"), torch.randn(8, 8, device="cuda").half(), 3)
 
@@ -206,6 +270,19 @@ def test_capi_matches_torch_ops():
     ext.capi_check(lib.kpb_matmul(3, 2, _p(a), _p(b), _p(c), 256, 300, 128, stream))
     torch.cuda.synchronize()
     assert torch.equal(c, ops.matmul(a, b, 3))
+
+    a, b = get_spec("vector_add").make_inputs((100_001,), torch.bfloat16, dev, 0)
+    c = torch.empty_like(a)
+    ext.capi_check(lib.kpb_vector_add(2, 2, _p(a), _p(b), _p(c), a.numel(), stream))
+    torch.cuda.synchronize()
+    assert torch.equal(c, ops.vector_add(a, b, 2))
+
+    x, w, b = get_spec("layernorm").make_inputs((100, 3000), torch.float16, dev, 0)
+    y = torch.empty_like(x)
+    ext.capi_check(lib.kpb_layernorm(2, 1, _p(x), _p(w), _p(b), _p(y), 100, 3000,
+                                     ctypes.c_float(1e-5), stream))
+    torch.cuda.synchronize()
+    assert torch.equal(y, ops.layernorm(x, w, b, 1e-5, 2))
 
     q, k, v = get_spec("attention").make_inputs((1, 2, 200, 128), torch.bfloat16, dev, 0)
     o = torch.empty_like(q)

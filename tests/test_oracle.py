@@ -14,7 +14,8 @@ import torch
 from oracle import oracle
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-OPS = ["reduce_sum", "softmax", "matmul", "attention", "attention_causal"]
+OPS = ["vector_add", "reduce_sum", "softmax", "matmul", "layernorm", "attention",
+       "attention_causal"]
 
 
 def golden_cases(op: str):
