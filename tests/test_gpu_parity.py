@@ -117,6 +117,9 @@ EDGE = [
     ("matmul", (2049, 4097, 2048), torch.bfloat16),
     # ragged everything in fp16 (N % 256 = 76, K % 64 = 8)
     ("matmul", (777, 1100, 5000), torch.float16),
+    # A rows not 16-byte aligned (K % 8 = 7): A staged alone, then A and B both staged
+    ("matmul", (256, 512, 999), torch.float16),
+    ("matmul", (300, 500, 1001), torch.bfloat16),
     ("attention", (2, 3, 300, 128), torch.bfloat16),
     ("attention", (1, 4, 513, 64), torch.float16),
     ("attention_causal", (2, 3, 300, 128), torch.bfloat16),
@@ -134,6 +137,20 @@ EDGE = [
                          ids=[f"{k}-{s}-{str(d)[6:]}" for k, s, d in EDGE])
 def test_edge_shapes_best_variant(kernel, shape, dtype):
     res = check_impl(get_spec(kernel), "best", registry.best(kernel), shape, dtype, "cuda")
+    assert res.ok, res.summary()
+
+
+@pytest.mark.parametrize("a_off,b_off", [(1, 0), (0, 3), (5, 2)])
+def test_matmul_misaligned_bases(a_off, b_off):
+    # a base off a 16-byte boundary cannot be a TMA base: that operand is staged
+    spec = get_spec("matmul")
+    dev = torch.device("cuda")
+    M, N, K = 384, 520, 640
+    a0, b0 = spec.make_inputs((M + 1, N + 1, K + 1), torch.bfloat16, dev, 0)
+    a = a0.flatten()[a_off:a_off + M * K].view(M, K)
+    b = b0.flatten()[b_off:b_off + K * N].view(K, N)
+    res = check_on_inputs(spec, "best", registry.best("matmul"), (a, b), (M, N, K),
+                          torch.bfloat16)
     assert res.ok, res.summary()
 
 
