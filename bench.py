@@ -172,13 +172,30 @@ def physical_gpu_index(local_rank: int) -> int:
 
 # ------------------------------------------------------------------ op plumbing
 
-def make_step(w: Workload, inputs: tuple, rk: kdist.Rank):
+def reduce_exchange(rk: kdist.Rank):
+    """(callable, description) of the reduction's exchange step at world > 1: the
+    in-kernel peer-memory combine when every rank can map its peers' memory, else one
+    NCCL all_reduce of the fp32 partial (decided collectively)."""
+    from kernelpilot_b200 import registry
+
+    fn = registry.best("reduce_sum")
+    if rk.world > 1:
+        try:
+            return kdist.PeerSum(), "in the finishing kernel: partials stored into every " \
+                "rank's buffer over NVLink (CUDA IPC), summed in rank order"
+        except RuntimeError:
+            pass
+    return (lambda x: kdist.sharded_reduce_sum(x, fn)), "all_reduce(SUM) of fp32 partials"
+
+
+def make_step(w: Workload, inputs: tuple, rk: kdist.Rank, exchange=None):
     """The timed unit: one call of the best variant (+ the exchange step, if any)."""
     from kernelpilot_b200 import registry
 
     fn = registry.best(w.kernel)
     if w.kernel == "reduce_sum":
-        return lambda: kdist.sharded_reduce_sum(inputs[0], fn)
+        ex = exchange or (lambda x: kdist.sharded_reduce_sum(x, fn))
+        return lambda: ex(inputs[0])
     return lambda: fn(*inputs)
 
 
@@ -211,7 +228,7 @@ def time_steps(step, steps: int, flush: bool, rk: kdist.Rank) -> tuple[float, li
     return float(total.item()), per
 
 
-def time_e2e(w: Workload, dev_inputs: tuple, steps: int, rk: kdist.Rank) -> dict:
+def time_e2e(w: Workload, dev_inputs: tuple, steps: int, rk: kdist.Rank, exchange=None) -> dict:
     """Public API with host buffers: H2D of the step's inputs from pinned memory, the
     op, D2H of its result, all inside the timed region."""
     from kernelpilot_b200 import registry
@@ -227,7 +244,7 @@ def time_e2e(w: Workload, dev_inputs: tuple, steps: int, rk: kdist.Rank) -> dict
         for d, h in zip(dev, host, strict=True):
             d.copy_(h, non_blocking=True)
         if w.kernel == "reduce_sum":
-            r = kdist.sharded_reduce_sum(dev[0], fn)
+            r = (exchange or (lambda x: kdist.sharded_reduce_sum(x, fn)))(dev[0])
         else:
             r = fn(*dev)
         if out_host is None:
@@ -390,7 +407,9 @@ def main() -> int:
     inputs = w.inputs("cuda", seed=rk.rank)
     in_bytes = sum(t.numel() * t.element_size() for t in inputs)
     flush = in_bytes < 2 * L2_BYTES
-    step = make_step(w, inputs, rk)
+    exchange, exchange_desc = (reduce_exchange(rk) if w.kernel == "reduce_sum" and rk.world > 1
+                               else (None, "all_reduce(SUM) of fp32 partials"))
+    step = make_step(w, inputs, rk, exchange)
 
     with ClockSampler(physical_gpu_index(rk.local_rank)) as clocks:
         for _ in range(args.warmup):
@@ -411,7 +430,7 @@ def main() -> int:
             "peak_source": f"{peak_src} (MEASURED_PEAKS.json)" if peak_src == "measured"
             else "fallback"}
 
-    e2e = time_e2e(w, inputs, args.e2e_steps, rk) if args.e2e_steps > 0 else None
+    e2e = time_e2e(w, inputs, args.e2e_steps, rk, exchange) if args.e2e_steps > 0 else None
 
     configs = {}
     if rk.world == 1 and not args.no_configs:
@@ -431,6 +450,10 @@ def main() -> int:
 
     if rk.world > 1:
         torch.distributed.barrier()
+        torch.cuda.synchronize()
+        if isinstance(exchange, kdist.PeerSum):
+            torch.distributed.barrier()  # no rank still writes into a peer's buffer
+            exchange.close()
         torch.distributed.destroy_process_group()
     if rk.rank != 0:
         return 0
@@ -443,8 +466,8 @@ def main() -> int:
         "config": {"workload": w.key, "shape": list(w.shape), "description": w.description,
                    "per_rank": "one full instance per GPU",
                    "l2": "flushed between steps outside the events (256 MB written, then read so no dirty lines remain)" if flush else "inputs larger than L2",
-                   "exchange": "all_reduce(SUM) of fp32 partials" if w.kernel == "reduce_sum"
-                   else "none", "parallelism": f"dp{rk.world}"},
+                   "exchange": (exchange_desc if rk.world > 1 else "none (one GPU)")
+                   if w.kernel == "reduce_sum" else "none", "parallelism": f"dp{rk.world}"},
         "pct_of_peak": round(value * (1e3 if w.bound == "hbm" else 1.0) / (peak * rk.world), 4),
         "roofline": roof,
         "e2e": ({k: (round(v, 5) if isinstance(v, float) else v) for k, v in e2e.items()}

@@ -84,6 +84,30 @@ int kpb_reduce_sum_ws(int variant, int dtype, const void* x, float* out, int64_t
  * is made. */
 int kpb_reduce_sum_noalloc(int dtype, const void* x, float* out, int64_t n, void* stream);
 
+/* ---- full sum over the GPUs of one node, exchange in the kernel: replaces the
+ * all_reduce step of the data-parallel reduction (the reference has no multi-GPU
+ * code; on one GPU its reduction ends in atomicAdd, csrc/kernels/reduction.hip:86) ----
+ * One process per GPU, each holding its shard of the vector. Once per process:
+ * kpb_peer_sum_create exports this rank's small exchange buffer as a CUDA IPC handle
+ * (kpb_peer_sum_handle_bytes() bytes); the caller gathers every rank's handle in rank
+ * order (any host-side all_gather) and passes them to kpb_peer_sum_connect. Then every
+ * rank calls kpb_peer_sum_run the same number of times, in the same order: each call
+ * reduces the local shard (the persistent kernel; partials in the caller's workspace
+ * of kpb_peer_sum_workspace_bytes(n) bytes) and its one-CTA finishing kernel stores
+ * the local sum into every rank's buffer over NVLink, waits (bounded) for the other
+ * ranks' sums and writes out[0] = sum over ranks in rank order: the same bits on every
+ * rank. A rank that never arrives makes the others set the timeout bit of
+ * kpb_device_errors() and write NaN. At most 8 ranks; all on one node with
+ * peer access (NVLink/NVSwitch). */
+typedef struct kpb_peer_sum kpb_peer_sum;
+size_t kpb_peer_sum_handle_bytes(void);
+int kpb_peer_sum_create(int rank, int world, void* ipc_handle_out, kpb_peer_sum** out);
+int kpb_peer_sum_connect(kpb_peer_sum* ps, const void* all_handles);
+size_t kpb_peer_sum_workspace_bytes(int64_t n);
+int kpb_peer_sum_run(kpb_peer_sum* ps, int dtype, const void* x, float* out, int64_t n,
+                     void* workspace, size_t workspace_bytes, void* stream);
+int kpb_peer_sum_destroy(kpb_peer_sum* ps);
+
 /* ---- row softmax: replaces kp::softmax (csrc/launchers.h:17-18) ----
  * y = softmax(x) over the last dimension of a contiguous (M, N) matrix;
  * fp32 math for every dtype; M, N < 2^31. */

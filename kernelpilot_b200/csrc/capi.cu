@@ -64,7 +64,7 @@ int sm_count() {
 }
 
 // Device address of this device's error word (looked up once per device).
-static int device_error_word(unsigned** out) {
+int device_error_word(unsigned** out) {
   int dev = 0;
   KPB_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return fail(KPB_EUNSUPPORTED, "device index out of range");

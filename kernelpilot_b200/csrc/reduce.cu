@@ -143,9 +143,12 @@ int64_t level1_ctas(int variant, int64_t n, int sms) {
   return std::max<int64_t>(1, std::min<int64_t>(int64_t(sms) * kVecCtasPerSm, want));
 }
 
+// Level 1 of `variant`: one partial per CTA into partials[0 .. *ctas).
 template <typename T>
-int launch(int variant, const T* x, float* out, int64_t n, float* partials, cudaStream_t s) {
+int launch_level1(int variant, const T* x, int64_t n, float* partials, int64_t* ctas_out,
+                  cudaStream_t s) {
   const int64_t ctas = level1_ctas(variant, n, sm_count());
+  *ctas_out = ctas;
   if (variant == 0) {
     sum_chunked<T><<<static_cast<unsigned>(ctas), kChunkThreads, 0, s>>>(x, partials, n);
   } else if (variant == 1) {
@@ -159,7 +162,13 @@ int launch(int variant, const T* x, float* out, int64_t n, float* partials, cuda
         x, partials, n, static_cast<int>(head));
   }
   KPB_LAUNCHED("reduce_sum level 1");
+  return KPB_OK;
+}
 
+template <typename T>
+int launch(int variant, const T* x, float* out, int64_t n, float* partials, cudaStream_t s) {
+  int64_t ctas = 0;
+  if (int rc = launch_level1(variant, x, n, partials, &ctas, s)) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(kFinishThreads);
@@ -185,6 +194,19 @@ size_t reduce_workspace_bytes(int variant, int64_t n) {
   // variant 2's CTA count depends on the SM count; size for the largest B200-class part
   const int64_t ctas = variant == 2 ? int64_t(kVecCtasPerSm) * 256 : level1_ctas(variant, n, 256);
   return static_cast<size_t>(ctas) * sizeof(float);
+}
+
+// Level 1 of the persistent variant alone (n > 0): the partials for a caller that
+// finishes the sum itself. partials must hold reduce_partials_needed(2, n) floats.
+int reduce_level1_persistent(int dtype, const void* x, int64_t n, float* partials,
+                             int64_t* ctas, cudaStream_t s) {
+  switch (dtype) {
+    case KPB_F32: return launch_level1(2, static_cast<const float*>(x), n, partials, ctas, s);
+    case KPB_F16: return launch_level1(2, static_cast<const __half*>(x), n, partials, ctas, s);
+    case KPB_BF16:
+      return launch_level1(2, static_cast<const __nv_bfloat16*>(x), n, partials, ctas, s);
+    default: return fail(KPB_EINVAL, "reduce_sum: unknown dtype " + std::to_string(dtype));
+  }
 }
 
 int reduce_sum(int variant, int dtype, const void* x, float* out, int64_t n, void* ws,

@@ -3,7 +3,9 @@
 The reference has no multi-GPU code. Here every headline workload partitions into
 independent units, and the only exchange steps are the ones the math needs:
 
-    reduce_sum        contiguous chunks; local fp32 partial -> all_reduce(SUM)
+    reduce_sum        contiguous chunks; the per-GPU sums are exchanged inside the
+                      finishing kernel over NVLink peer memory (PeerSum), or by an
+                      all_reduce(SUM) of the fp32 partial (sharded_reduce_sum)
     softmax           row blocks; no collective (all_gather only to assemble)
     matmul            M-blocks of A (B replicated); all_gather of C only to assemble
     attention(_causal) (B*H) slices; all_gather of O only to assemble
@@ -14,6 +16,7 @@ Ops are passed in as callables so the same host logic runs the CUDA kernels on G
 
 from __future__ import annotations
 
+import ctypes
 import datetime
 import os
 from collections.abc import Callable
@@ -73,6 +76,77 @@ def sharded_reduce_sum(x_local: torch.Tensor, op: Callable[[torch.Tensor], torch
     if dist.is_initialized() and dist.get_world_size() > 1:
         dist.all_reduce(part, op=dist.ReduceOp.SUM)
     return part.reshape(())
+
+
+class PeerSum:
+    """Global sum of a vector sharded over this node's GPUs, with the exchange step
+    inside the finishing kernel over NVLink peer memory (``kpb_peer_sum_*``): each
+    call reduces the local shard and the one-CTA finishing kernel stores its sum into
+    every rank's exchange buffer, waits (bounded) for the others and adds them in rank
+    order, so every rank gets the same bits and no collective is launched.
+
+    Construction is collective (every rank of the process group must construct it, in
+    the same order as its other collectives): the ranks export their exchange buffers
+    as CUDA IPC handles, agree that all exports worked (else every rank raises and the
+    caller can fall back to ``sharded_reduce_sum``) and all-gather the handles. Calls
+    must then be made by every rank, the same number of times, in the same order.
+    """
+
+    def __init__(self, group=None):
+        from . import ext
+
+        self._lib = lib = ext.capi()
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        nb = lib.kpb_peer_sum_handle_bytes()
+        handle = ctypes.create_string_buffer(nb)
+        self._ps = ctypes.c_void_p()
+        rc = lib.kpb_peer_sum_create(rank, world, handle, ctypes.byref(self._ps))
+        msg = lib.kpb_last_error().decode() if rc else ""
+        dev = torch.device("cuda", torch.cuda.current_device())
+        if world > 1:
+            ok = torch.tensor([1 if rc == 0 else 0], device=dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+            if int(ok.item()) == 0:
+                self.close()
+                raise RuntimeError(f"peer sum unavailable on some rank ({msg or 'another rank'})")
+            mine = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).to(dev)
+            every = torch.empty(world * nb, dtype=torch.uint8, device=dev)
+            dist.all_gather_into_tensor(every, mine, group=group)
+            raw = bytes(every.cpu().tolist())
+        else:
+            if rc:
+                raise RuntimeError(f"peer sum unavailable: {msg}")
+            raw = handle.raw
+        rc = lib.kpb_peer_sum_connect(self._ps, raw)
+        if rc:
+            msg = lib.kpb_last_error().decode()
+            self.close()
+            raise RuntimeError(f"peer sum connect failed: {msg}")
+        self._ws = torch.empty(0, dtype=torch.uint8, device=dev)
+
+    def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
+        from . import ext
+
+        x = x_local.reshape(-1)
+        if not x.is_contiguous():
+            x = x.contiguous()
+        n = x.numel()
+        need = self._lib.kpb_peer_sum_workspace_bytes(n)
+        if self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+        out = torch.empty((), dtype=torch.float32, device=x.device)
+        ext.capi_check(self._lib.kpb_peer_sum_run(
+            self._ps, ext.DTYPE_CODES[x.dtype], x.data_ptr(), out.data_ptr(), n,
+            self._ws.data_ptr(), self._ws.numel(), ext.current_stream_ptr(x.device)))
+        return out
+
+    def close(self) -> None:
+        """Release the exchange buffer and the peers' mappings (after a barrier, so no
+        rank still writes into them)."""
+        if getattr(self, "_ps", None) is not None and self._ps.value:
+            self._lib.kpb_peer_sum_destroy(self._ps)
+        self._ps = None
 
 
 def assemble_rows(local: torch.Tensor, counts: list[int]) -> torch.Tensor:

@@ -69,6 +69,12 @@ CAPI_SIGNATURES: dict[str, tuple] = {
     "kpb_reduce_sum_workspace_bytes": (_sz, [_i32, _i64]),
     "kpb_reduce_sum_ws": (_i32, [_i32, _i32, _vp, _vp, _i64, _vp, _sz, _vp]),
     "kpb_reduce_sum_noalloc": (_i32, [_i32, _vp, _vp, _i64, _vp]),
+    "kpb_peer_sum_handle_bytes": (_sz, []),
+    "kpb_peer_sum_create": (_i32, [_i32, _i32, _vp, ctypes.POINTER(_vp)]),
+    "kpb_peer_sum_connect": (_i32, [_vp, _vp]),
+    "kpb_peer_sum_workspace_bytes": (_sz, [_i64]),
+    "kpb_peer_sum_run": (_i32, [_vp, _i32, _vp, _vp, _i64, _vp, _sz, _vp]),
+    "kpb_peer_sum_destroy": (_i32, [_vp]),
     "kpb_softmax": (_i32, [_i32, _i32, _vp, _vp, _i64, _i64, _vp]),
     "kpb_matmul": (_i32, [_i32, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "kpb_matmul_workspace_bytes": (_sz, [_i32, _i32, _i64, _i64, _i64]),

@@ -89,6 +89,22 @@ def test_workspace_queries(lib):
 def test_ctypes_types_are_plain():
     # the boundary has no torch types: every argument is an int, a float, a size or a pointer
     allowed = {ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_float,
-               ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint)}
+               ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_void_p)}
     for _name, (_res, args) in ext.CAPI_SIGNATURES.items():
         assert all(a in allowed for a in args)
+
+
+def test_peer_sum_rejects_bad_arguments_without_a_gpu(lib):
+    # argument checks come before any CUDA call
+    handle = ctypes.create_string_buffer(lib.kpb_peer_sum_handle_bytes())
+    ps = ctypes.c_void_p()
+    assert lib.kpb_peer_sum_handle_bytes() == 64  # a cudaIpcMemHandle_t
+    assert lib.kpb_peer_sum_create(0, 9, handle, ctypes.byref(ps)) == 1
+    assert b"world" in lib.kpb_last_error()
+    assert lib.kpb_peer_sum_create(2, 2, handle, ctypes.byref(ps)) == 1
+    assert lib.kpb_peer_sum_create(0, 2, None, ctypes.byref(ps)) == 1
+    assert lib.kpb_peer_sum_connect(None, handle) == 1
+    assert lib.kpb_peer_sum_run(None, 0, None, None, 10, None, 0, None) == 1
+    assert lib.kpb_peer_sum_destroy(None) == 0
+    assert lib.kpb_peer_sum_workspace_bytes(0) == 0
+    assert lib.kpb_peer_sum_workspace_bytes(1 << 20) >= 4

@@ -1,0 +1,106 @@
+"""The full sum over GPUs with the exchange inside the finishing kernel (dist.PeerSum
+over kpb_peer_sum_*): on one GPU it equals kpb_reduce_sum bit for bit; on two GPUs
+(one process each, NCCL only to hand the IPC handles around) every rank gets the same
+bits, equal to the rank-ordered fp32 sum of the ranks' own reductions, on several calls
+in a row (both exchange rows); and a rank that skips a call makes the other rank's
+bounded wait give up with NaN and the timeout bit instead of hanging."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from kernelpilot_b200 import dist as kdist
+from kernelpilot_b200 import ext
+from kernelpilot_b200.specs import get_spec
+
+pytestmark = pytest.mark.gpu
+
+
+def _reduce(x):
+    out = torch.empty((), device=x.device)
+    ext.capi_check(ext.capi().kpb_reduce_sum(2, ext.DTYPE_CODES[x.dtype], x.data_ptr(),
+                                             out.data_ptr(), x.numel(),
+                                             ext.current_stream_ptr(x.device)))
+    return out
+
+
+def test_one_gpu_matches_the_allocating_reduction_bit_for_bit():
+    peer = kdist.PeerSum()
+    try:
+        spec = get_spec("reduce_sum")
+        for seed, n, dtype in [(0, 2**24 + 3, torch.float32), (1, 1_000_001, torch.bfloat16),
+                               (2, 7, torch.float16), (3, 2**24 + 3, torch.float32)]:
+            x = spec.make_inputs((n,), dtype, torch.device("cuda"), seed)[0]
+            got, want = peer(x), _reduce(x)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), (n, str(dtype), float(got), float(want))
+        empty = peer(torch.empty(0, device="cuda"))
+        torch.cuda.synchronize()
+        assert float(empty) == 0.0
+    finally:
+        peer.close()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _two_rank_worker(rank: int, world: int, port: int, results) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        spec = get_spec("reduce_sum")
+        peer = kdist.PeerSum()
+        for call in range(3):
+            x = spec.make_inputs((3_000_017 + rank,), torch.float32, torch.device("cuda"),
+                                 10 * call + rank)[0]
+            got = peer(x)
+            mine = _reduce(x)
+            both = [torch.empty((), device="cuda") for _ in range(world)]
+            dist.all_gather(both, mine)
+            want = both[0] + both[1]  # fp32, rank order
+            seen = [torch.empty((), device="cuda") for _ in range(world)]
+            dist.all_gather(seen, got)
+            torch.cuda.synchronize()
+            results[(rank, call)] = (got.item(), want.item(), seen[0].item(), seen[1].item())
+        # rank 1 skips the next call: rank 0's wait must give up, not hang
+        dist.barrier()
+        ext.capi().kpb_device_errors(None)  # clear the word
+        if rank == 0:
+            x = spec.make_inputs((1000,), torch.float32, torch.device("cuda"), 99)[0]
+            got = peer(x)
+            torch.cuda.synchronize()
+            word = ext.ctypes.c_uint(0)
+            ext.capi_check(ext.capi().kpb_device_errors(ext.ctypes.byref(word)))
+            results[(rank, "timeout")] = (got.item(), word.value)
+        torch.cuda.synchronize()
+        dist.barrier()
+        peer.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpus_agree_bit_for_bit_and_time_out_cleanly():
+    results = mp.get_context("spawn").Manager().dict()
+    mp.spawn(_two_rank_worker, args=(2, _free_port(), results), nprocs=2, join=True)
+    for call in range(3):
+        for rank in range(2):
+            got, want, s0, s1 = results[(rank, call)]
+            assert got == want, (rank, call, got, want)
+            assert s0 == s1  # the same bits on both ranks
+    got, word = results[(0, "timeout")]
+    assert got != got  # NaN
+    assert word & 1  # the timeout bit of the device error word
