@@ -119,10 +119,16 @@ class PeerSum:
                 raise RuntimeError(f"peer sum unavailable: {msg}")
             raw = handle.raw
         rc = lib.kpb_peer_sum_connect(self._ps, raw)
+        msg = lib.kpb_last_error().decode() if rc else ""
+        if world > 1:
+            # every rank must take the same path: fail together if any rank could not
+            # map its peers
+            ok = torch.tensor([1 if rc == 0 else 0], device=dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+            rc = 0 if int(ok.item()) == 1 else (rc or 1)
         if rc:
-            msg = lib.kpb_last_error().decode()
             self.close()
-            raise RuntimeError(f"peer sum connect failed: {msg}")
+            raise RuntimeError(f"peer sum connect failed on some rank ({msg or 'another rank'})")
         self._ws = torch.empty(0, dtype=torch.uint8, device=dev)
 
     def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
