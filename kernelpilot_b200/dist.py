@@ -103,7 +103,8 @@ class PeerSum:
         self._ps = ctypes.c_void_p()
         rc = lib.kpb_peer_sum_create(rank, world, handle, ctypes.byref(self._ps))
         msg = lib.kpb_last_error().decode() if rc else ""
-        dev = torch.device("cuda", torch.cuda.current_device())
+        dev = (torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available()
+               else torch.device("cpu"))
         if world > 1:
             ok = torch.tensor([1 if rc == 0 else 0], device=dev)
             dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)

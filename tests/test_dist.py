@@ -68,3 +68,39 @@ def test_two_gloo_ranks_combine_partials_and_assemble_rows():
         assert total != "error", want
         assert abs(total - want) < 1e-3, (rank, total, want)
         assert assembled
+
+
+def _fallback_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    try:
+        kdist.init(backend="gloo", timeout_s=30)
+        # no rank can export an exchange buffer here (no GPU): every rank must learn it
+        # in the same collective and raise, so all can fall back to the all_reduce
+        try:
+            kdist.PeerSum()
+            outcome = "constructed"
+        except RuntimeError as e:
+            outcome = str(e)
+        x = torch.full((10,), float(rank + 1))
+        total = kdist.sharded_reduce_sum(x, lambda t: t.sum(dtype=torch.float32))
+        dist.barrier()
+        q.put((rank, outcome, float(total)))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, "error", repr(e)))
+
+
+def test_peer_sum_unavailable_on_every_rank_falls_back_together():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fallback_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, outcome, total in results:
+        assert outcome.startswith("peer sum unavailable"), (rank, outcome, total)
+        assert total == 30.0  # 10 * 1 + 10 * 2 on both ranks, through the fallback
