@@ -355,14 +355,15 @@ def run_reference(args, rk: kdist.Rank) -> int:
 
 # ------------------------------------------------------------------ main
 
-def quick_measure(w: Workload, rk: kdist.Rank, steps: int = 10, warmup: int = 3) -> dict:
-    """Device-side rate of another workload on this GPU (for the configs table)."""
+def quick_measure(w: Workload, rk: kdist.Rank, steps: int = 30, warmup: int = 3) -> dict:
+    """Device-side rate of another workload on this GPU (for the configs table): the
+    rate over the mean of `steps` timed calls, with the median call time beside it."""
     inputs = w.inputs("cuda", seed=0)
     step = make_step(w, inputs, kdist.Rank(0, 1, rk.local_rank))
     for _ in range(warmup):
         step()
     flush = sum(t.numel() * t.element_size() for t in inputs) < 2 * L2_BYTES
-    total, _ = time_steps(step, steps, flush, kdist.Rank(0, 1, rk.local_rank))
+    total, per = time_steps(step, steps, flush, kdist.Rank(0, 1, rk.local_rank))
     ms = total / steps
     peak, src = roofline_peak(w)
     val = rate(w, ms)
@@ -370,6 +371,7 @@ def quick_measure(w: Workload, rk: kdist.Rank, steps: int = 10, warmup: int = 3)
     del inputs
     torch.cuda.empty_cache()
     return {"value": round(val, 4), "unit": unit_of(w), "ms": round(ms, 5),
+            "ms_median": round(statistics.median(per), 5), "steps": steps,
             "frac_of_peak": round(val * scale / peak, 4), "peak_source": src}
 
 
