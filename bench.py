@@ -419,6 +419,17 @@ def main() -> int:
         torch.cuda.synchronize()
         total_ms, per = time_steps(step, args.steps, flush, rk)
     ms = total_ms / args.steps
+    if w.kernel == "reduce_sum":
+        # one more call on every rank, outside the timing: the sum must be finite and no
+        # bounded wait (the peer exchange) may have given up during the run
+        import ctypes
+
+        check = float(step())
+        word = ctypes.c_uint(0)
+        ext.capi_check(ext.capi().kpb_device_errors(ctypes.byref(word)))
+        if not math.isfinite(check) or word.value:
+            raise RuntimeError(f"reduce_sum run invalid: result {check}, device error bits "
+                               f"{word.value:#x}")
     value = rate(w, ms) * rk.world
     peak, peak_src = roofline_peak(w)
     # dominant kernel: the op's own launches, timed per call on the op's stream
