@@ -446,16 +446,21 @@ def main() -> int:
     e2e = time_e2e(w, inputs, args.e2e_steps, rk, exchange) if args.e2e_steps > 0 else None
 
     configs = {}
+    configs_clocks = None
     if rk.world == 1 and not args.no_configs:
         del inputs, step
         torch.cuda.empty_cache()
-        for key, other in CONFIGS.items():
-            if key == w.key:
-                continue
-            try:
-                configs[key] = quick_measure(other, rk)
-            except Exception as e:  # reported in the line, never hidden
-                configs[key] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        # clocks sampled over the whole table too: its numbers are only comparable
+        # between runs at the same clocks
+        with ClockSampler(physical_gpu_index(rk.local_rank)) as table_clocks:
+            for key, other in CONFIGS.items():
+                if key == w.key:
+                    continue
+                try:
+                    configs[key] = quick_measure(other, rk)
+                except Exception as e:  # reported in the line, never hidden
+                    configs[key] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        configs_clocks = table_clocks.summary()
 
     cpu = None
     if rk.world == 1 and rk.rank == 0 and not args.no_cpu:
@@ -493,6 +498,7 @@ def main() -> int:
                                 for k, v in cpu.items()}
     if configs:
         line["configs"] = configs
+        line["configs_clocks"] = configs_clocks
     print(json.dumps(line), flush=True)
     return 0
 
