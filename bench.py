@@ -157,7 +157,8 @@ class ClockSampler:
             for name, val in zip(names, parts[5:9], strict=False):
                 if val.lower() == "active":
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_mhz_min": min(sm) if sm else None, "sm_max_mhz": smax,
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
@@ -355,13 +356,27 @@ def run_reference(args, rk: kdist.Rank) -> int:
 
 # ------------------------------------------------------------------ main
 
-def quick_measure(w: Workload, rk: kdist.Rank, steps: int = 30, warmup: int = 3) -> dict:
+def quick_measure(w: Workload, rk: kdist.Rank, warmup: int = 3, budget_ms: float = 5.0,
+                  min_steps: int = 10, max_steps: int = 50) -> dict:
     """Device-side rate of another workload on this GPU (for the configs table): the
-    rate over the mean of `steps` timed calls, with the median call time beside it."""
+    rate over the mean of the timed calls, with the median call time beside it. The
+    number of calls fills about `budget_ms` of device time (within [min_steps,
+    max_steps]), estimated from the warm-up: short kernels get enough calls for a
+    stable mean, long tensor-core ones few enough that the table does not push the
+    GPU into power capping and slow the rows after them."""
     inputs = w.inputs("cuda", seed=0)
     step = make_step(w, inputs, kdist.Rank(0, 1, rk.local_rank))
     for _ in range(warmup):
         step()
+    # the estimate comes from calls after the warm-up (first calls carry one-time costs)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(2):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    est = max(t0.elapsed_time(t1) / 2, 1e-3)
+    steps = int(min(max_steps, max(min_steps, budget_ms / est)))
     flush = sum(t.numel() * t.element_size() for t in inputs) < 2 * L2_BYTES
     total, per = time_steps(step, steps, flush, kdist.Rank(0, 1, rk.local_rank))
     ms = total / steps
