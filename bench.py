@@ -3,24 +3,32 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload KEY] [--impl ours|reference]
 
-A step is one call of the op on one full-size synthetic instance of the workload
-(default: full sum of 2^28+1 fp32 values drawn U(-1,1), the reduction headline
-configuration). Under torchrun each rank is one GPU holding its own instance (weak
-scaling: the job is N instances); ops whose math needs an exchange step run it over
-NCCL inside the timed step (reduce_sum: all_reduce of the fp32 partials).
+A step is one call of the op on the whole synthetic job (default: full sum of one
+vector of 2^28+1 fp32 values drawn U(-1,1), the reduction headline configuration).
+Under torchrun the ONE job is split N ways along the op's natural axis (strong
+scaling): the reduction into contiguous chunks, softmax and LayerNorm into row
+blocks, GEMM into M-blocks of A with B replicated, attention into (batch, head)
+slices. Every rank draws the same global input from the same seed and keeps its
+shard. The reduction's one exchange step (the sum of the per-GPU partials) runs in
+its finishing kernel over NVLink peer memory inside the timed step; the other ops
+need no exchange (an all_gather would only assemble outputs).
 
-value      whole-job algorithmic bytes (or FLOPs) / max-over-ranks device time,
-           inputs resident in HBM; per-step CUDA events; when the working set fits
-           in L2, L2 is flushed between steps outside the events (a 256 MB buffer
+value      whole-job algorithmic bytes (or FLOPs) / max-over-ranks device time, inputs
+           resident in HBM; per-step CUDA events; when a rank's working set is under
+           twice the L2, L2 is flushed between steps outside the events (256 MB
            written, then read back so no dirty lines are left for the timed kernel).
-e2e        the same metric through the public API (torch.ops.kp) with the inputs
-           copied from pinned host memory and the result copied back inside the
-           timed region.
-roofline   the op's algorithmic bytes/FLOPs per call over its measured device time,
+e2e        the same metric through the public API (torch.ops.kp, and the peer-sum
+           object at N > 1) with each rank's inputs copied from pinned host memory and
+           the result copied back inside the timed region.
+roofline   rank 0's algorithmic bytes/FLOPs per call over its measured device time,
            against MEASURED_PEAKS.json (HBM copy GB/s, or cuBLAS bf16 TFLOP/s).
+check      the reduction's result against the float64 sum of the global vector (the
+           ranks' float64 shard sums, all-reduced), with the spec's tolerance.
+configs    the other headline workloads, split the same way, device-timed; at N = 1
+           each row also carries its e2e number and the reference's CPU path.
 cpu_baseline  the reference's CPU path (the PyTorch built-in its spec names as
            ``baseline``) on this box's host cores, rank 0 at N=1 only.
---impl reference  runs only that CPU path, on the same workload, and prints its line.
+--impl reference  runs only that CPU path, on the same job, and prints its line.
 """
 
 from __future__ import annotations
@@ -49,11 +57,13 @@ METRIC = json.loads((REPO / "BASELINE.json").read_text())["metric"] \
     "achieved HBM TB/s (softmax/reduce) and BF16 TFLOPS (GEMM/attn), % of peak"
 DEFAULT_WORKLOAD = "reduce_f32_2p28p1"
 L2_BYTES = 126 * 1024 * 1024
-# kernel launches of ours per op call (the op's level-1 kernel + finish, or one kernel)
+DTYPE_NAMES = {torch.float32: "f32", torch.float16: "f16", torch.bfloat16: "bf16"}
+
+
 def launches_per_call(w: Workload) -> int:
     """Kernels of ours one call of the best variant launches on this workload."""
     if w.kernel == "reduce_sum":
-        return 2  # persistent level + one-CTA finish
+        return 2  # persistent level + one-CTA finish (with the peer exchange at N > 1)
     if w.kernel == "matmul":
         M, N, K = w.shape
         # tensor-core GEMM, plus a pitch-padding copy per operand TMA cannot describe
@@ -61,7 +71,6 @@ def launches_per_call(w: Workload) -> int:
     if w.kernel == "attention_causal":
         return 2 if w.shape[2] > 256 else 1  # main grid + the few-key-rows grid
     return 1
-DTYPE_NAMES = {torch.float32: "f32", torch.float16: "f16", torch.bfloat16: "bf16"}
 
 
 # ------------------------------------------------------------------ helpers
@@ -80,6 +89,21 @@ def rate(w: Workload, ms: float) -> float:
     return work_per_call(w) / (ms / 1e3) / 1e12
 
 
+def local_workload(w: Workload, rank: int, world: int) -> Workload:
+    """The shard of the job this rank computes, as a workload of its own shape."""
+    import dataclasses
+
+    return dataclasses.replace(w, shape=kdist.local_shape(w.kernel, w.shape, rank, world))
+
+
+def job_config(w: Workload, world: int) -> dict:
+    """The ``config`` of the JSON line; both arms print exactly this dict."""
+    shapes = sorted({kdist.local_shape(w.kernel, w.shape, r, world) for r in range(world)})
+    return {"workload": w.key, "shape": list(w.shape), "dtype": DTYPE_NAMES[w.dtype],
+            "description": w.description, "partition": kdist.PARTITION[w.kernel],
+            "per_rank": [list(s) for s in shapes], "parallelism": f"dp{world}"}
+
+
 def measured_peaks() -> dict:
     try:
         return json.loads((REPO / "MEASURED_PEAKS.json").read_text())
@@ -92,10 +116,10 @@ def roofline_peak(w: Workload) -> tuple[float, str]:
     mp = measured_peaks()
     if w.bound == "hbm":
         if "hbm_gbs" in mp:
-            return float(mp["hbm_gbs"]), "measured"
+            return float(mp["hbm_gbs"]), "measured copy bandwidth (read + write)"
         return 6650.0, "fallback"
     if "bf16_tflops" in mp:
-        return float(mp["bf16_tflops"]), "measured"
+        return float(mp["bf16_tflops"]), "measured cuBLAS bf16 GEMM, burst"
     return 1590.0, "fallback"
 
 
@@ -110,6 +134,10 @@ def profiled_traffic(w: Workload) -> float | None:
     return float(m.group(1)) if m else None
 
 
+def rounded(d: dict, nd: int = 5) -> dict:
+    return {k: (round(v, nd) if isinstance(v, float) else v) for k, v in d.items()}
+
+
 class ClockSampler:
     """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
 
@@ -120,6 +148,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
         self.proc = None
+        self.out = ""
 
     def __enter__(self):
         try:
@@ -132,7 +161,6 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -145,7 +173,7 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in (getattr(self, "out", "") or "").splitlines():
+        for line in (self.out or "").splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -174,7 +202,7 @@ def physical_gpu_index(local_rank: int) -> int:
 # ------------------------------------------------------------------ op plumbing
 
 def reduce_exchange(rk: kdist.Rank):
-    """(callable, description) of the reduction's exchange step at world > 1: the
+    """(callable, description) of the reduction over the shards at world > 1: the
     in-kernel peer-memory combine when every rank can map its peers' memory, else one
     NCCL all_reduce of the fp32 partial (decided collectively)."""
     from kernelpilot_b200 import registry
@@ -189,24 +217,24 @@ def reduce_exchange(rk: kdist.Rank):
     return (lambda x: kdist.sharded_reduce_sum(x, fn)), "all_reduce(SUM) of fp32 partials"
 
 
-def make_step(w: Workload, inputs: tuple, rk: kdist.Rank, exchange=None):
-    """The timed unit: one call of the best variant (+ the exchange step, if any)."""
+def make_step(w: Workload, inputs: tuple, exchange=None):
+    """The timed unit: one call of the best variant on this rank's shard (+ the
+    exchange step of the reduction, if any)."""
     from kernelpilot_b200 import registry
 
     fn = registry.best(w.kernel)
-    if w.kernel == "reduce_sum":
-        ex = exchange or (lambda x: kdist.sharded_reduce_sum(x, fn))
-        return lambda: ex(inputs[0])
+    if w.kernel == "reduce_sum" and exchange is not None:
+        return lambda: exchange(inputs[0])
     return lambda: fn(*inputs)
 
 
-def time_steps(step, steps: int, flush: bool, rk: kdist.Rank) -> tuple[float, list[float]]:
+def time_steps(step, steps: int, flush: bool, world: int) -> tuple[float, list[float]]:
     """(max-over-ranks total ms of the K steps, per-step ms on this rank)."""
-    from kernelpilot_b200.benchmark import flush_l2
+    from kernelpilot_b200.harness import flush_l2
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    if rk.world > 1:
+    if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     for i in range(steps):
@@ -220,23 +248,24 @@ def time_steps(step, steps: int, flush: bool, rk: kdist.Rank) -> tuple[float, li
         step()
         ends[i].record()
     torch.cuda.synchronize()
-    if rk.world > 1:
+    if world > 1:
         torch.distributed.barrier()
     per = [s.elapsed_time(e) for s, e in zip(starts, ends, strict=True)]
     total = torch.tensor([sum(per)], dtype=torch.float64, device="cuda")
-    if rk.world > 1:
+    if world > 1:
         torch.distributed.all_reduce(total, op=torch.distributed.ReduceOp.MAX)
     return float(total.item()), per
 
 
-def time_e2e(w: Workload, dev_inputs: tuple, steps: int, rk: kdist.Rank, exchange=None) -> dict:
-    """Public API with host buffers: H2D of the step's inputs from pinned memory, the
-    op, D2H of its result, all inside the timed region."""
+def time_e2e(w: Workload, local: tuple, steps: int, world: int, exchange=None) -> dict:
+    """Public API with host buffers: H2D of this rank's inputs from pinned memory, the
+    op, D2H of its result, all inside the timed region; value = the whole job over the
+    max-over-ranks time."""
     from kernelpilot_b200 import registry
 
-    fn = registry.best(w.kernel)
-    host = [t.cpu().pin_memory() for t in dev_inputs]
-    dev = [torch.empty_like(t) for t in dev_inputs]
+    op = registry.best(w.kernel)
+    host = [t.cpu().pin_memory() for t in local]
+    dev = [torch.empty_like(t) for t in local]
     out_host = None
     h2d = sum(t.numel() * t.element_size() for t in host)
 
@@ -244,48 +273,65 @@ def time_e2e(w: Workload, dev_inputs: tuple, steps: int, rk: kdist.Rank, exchang
         nonlocal out_host
         for d, h in zip(dev, host, strict=True):
             d.copy_(h, non_blocking=True)
-        if w.kernel == "reduce_sum":
-            r = (exchange or (lambda x: kdist.sharded_reduce_sum(x, fn)))(dev[0])
-        else:
-            r = fn(*dev)
+        r = exchange(dev[0]) if (w.kernel == "reduce_sum" and exchange is not None) \
+            else op(*dev)
         if out_host is None:
             out_host = torch.empty(r.shape, dtype=r.dtype, pin_memory=True)
         out_host.copy_(r, non_blocking=True)
 
     one()
     torch.cuda.synchronize()
-    total, _ = time_steps(one, steps, flush=False, rk=rk)
+    total, _ = time_steps(one, steps, flush=False, world=world)
     d2h = out_host.numel() * out_host.element_size()
     ms = total / steps
-    return {"value": rate(w, ms) * rk.world, "unit": unit_of(w), "h2d_bytes_per_step": h2d,
+    del host, dev
+    return {"value": rate(w, ms), "unit": unit_of(w), "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms}
+
+
+def spot_check(w: Workload, local: tuple, out: torch.Tensor) -> dict:
+    """The reference gate (kernelpilot's ``compare`` with the spec's tolerance) on a
+    slice of this rank's output: 64 rows (softmax, LayerNorm, GEMM), one (batch,
+    head) slice (attention), the first 2^20 elements (elementwise add)."""
+    from kernelpilot_b200 import harness
+
+    spec = w.spec
+    if w.kernel in ("softmax", "layernorm"):
+        n = min(64, local[0].shape[0])
+        ins, got = (local[0][:n],) + tuple(local[1:]), out[:n]
+        shape = (n,) + tuple(w.shape[1:])
+    elif w.kernel == "matmul":
+        n = min(64, local[0].shape[0])
+        ins, got, shape = (local[0][:n], local[1]), out[:n], (n,) + tuple(w.shape[1:])
+    elif w.kernel in ("attention", "attention_causal"):
+        ins = tuple(t[:, :1] for t in local)
+        got, shape = out[:, :1], (1, 1) + tuple(w.shape[2:])
+    elif w.kernel == "vector_add":
+        n = min(1 << 20, local[0].numel())
+        ins, got, shape = tuple(t[:n] for t in local), out[:n], (n,)
+    else:
+        return {}
+    tol = spec.tolerance(shape, w.dtype)
+    info = harness.compare(got, spec.reference(*ins), tol.atol, tol.rtol)
+    return {"what": f"{tuple(got.shape)} slice of rank 0's output vs float64",
+            "max_abs_err": info["max_abs_err"], "ok": info["num_mismatched"] == 0}
 
 
 # ------------------------------------------------------------------ CPU (reference) path
 
 def reference_baseline(w: Workload):
-    """(callable, kind): the reference's CPU implementation of this op.
-
-    Preferred: the unmodified reference package installed under baseline/_ref, its
-    ``spec.baseline`` (the PyTorch built-in, kernelpilot/specs.py:127,158,200,274).
-    Else the same built-in through this package's mirror of the spec.
-    """
-    ref_dir = REPO / "baseline" / "_ref"
+    """(callable, kind): the reference's CPU implementation of this op: its
+    ``spec.baseline`` (the PyTorch built-in, kernelpilot/specs.py:127,158,200,274)
+    from the unmodified reference package the harness loads."""
     if w.kernel == "attention_causal":
-        # the reference has no causal op; its attention baseline with the causal flag
+        # the reference has no causal op: its attention baseline with the causal flag
         import torch.nn.functional as F
 
         return (lambda q, k, v: F.scaled_dot_product_attention(q, k, v, is_causal=True),
                 "reference")
-    if (ref_dir / "kernelpilot").exists():
-        sys.path.insert(0, str(ref_dir))
-        try:
-            from kernelpilot.specs import get_spec as ref_get_spec  # type: ignore
+    from kernelpilot_b200 import harness
 
-            return ref_get_spec(w.kernel).baseline, "reference"
-        except ImportError:
-            pass
-    return w.spec.baseline, "reference"
+    return harness.reference().specs.get_spec(w.kernel).baseline, "reference"
 
 
 def subset_workload(w: Workload, n: int) -> Workload:
@@ -342,53 +388,75 @@ def run_reference(args, rk: kdist.Rank) -> int:
         return 0
     w = CONFIGS[args.workload]
     cb = time_cpu(w, reps=args.steps + args.warmup)
-    line = {"metric": METRIC, "value": cb["value"], "unit": cb["unit"], "n_gpus": args.gpus,
+    line = {"metric": METRIC, "value": cb["value"], "unit": cb["unit"], "n_gpus": rk.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_call"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": DTYPE_NAMES[w.dtype], "data": "synthetic",
-            "config": {"workload": w.key, "shape": list(w.shape), "description": w.description},
-            "impl": "reference", "cpu_baseline": cb,
+            "higher_is_better": True, "scaling": "strong" if rk.world > 1 else "weak",
+            "vs_baseline": None, "dtype": DTYPE_NAMES[w.dtype], "data": "synthetic",
+            "config": job_config(w, rk.world),
+            "impl": "reference", "cpu_baseline": rounded(cb),
             "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
 
-# ------------------------------------------------------------------ main
+# ------------------------------------------------------------------ the configs table
 
-def quick_measure(w: Workload, rk: kdist.Rank, warmup: int = 3, budget_ms: float = 5.0,
-                  min_steps: int = 10, max_steps: int = 50) -> dict:
-    """Device-side rate of another workload on this GPU (for the configs table): the
-    rate over the mean of the timed calls, with the median call time beside it. The
-    number of calls fills about `budget_ms` of device time (within [min_steps,
-    max_steps]), estimated from the warm-up: short kernels get enough calls for a
+def measure_row(w: Workload, rk: kdist.Rank, with_host: bool, warmup: int = 3,
+                budget_ms: float = 5.0, min_steps: int = 10, max_steps: int = 50) -> dict:
+    """One workload of the table, split over the ranks like the headline: the whole
+    job's rate over the max-over-ranks mean call time, the median call time beside
+    it. The call count fills about ``budget_ms`` of device time (within [min_steps,
+    max_steps]), estimated after the warm-up: short kernels get enough calls for a
     stable mean, long tensor-core ones few enough that the table does not push the
-    GPU into power capping and slow the rows after them."""
-    inputs = w.inputs("cuda", seed=0)
-    step = make_step(w, inputs, kdist.Rank(0, 1, rk.local_rank))
+    GPU into power capping and slow the rows after it. ``with_host`` adds the row's
+    e2e number and the reference's CPU path (rank 0, one GPU)."""
+    world = rk.world
+    inputs = kdist.shard_inputs(w.kernel, w.inputs("cuda", seed=0), rk.rank, world)
+    torch.cuda.empty_cache()
+    exchange = reduce_exchange(rk)[0] if (w.kernel == "reduce_sum" and world > 1) else None
+    step = make_step(w, inputs, exchange)
     for _ in range(warmup):
         step()
-    # the estimate comes from calls after the warm-up (first calls carry one-time costs)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(2):
         step()
     t1.record()
     torch.cuda.synchronize()
-    est = max(t0.elapsed_time(t1) / 2, 1e-3)
-    steps = int(min(max_steps, max(min_steps, budget_ms / est)))
+    est = torch.tensor([max(t0.elapsed_time(t1) / 2, 1e-3)], device="cuda")
+    if world > 1:  # every rank must time the same number of calls
+        torch.distributed.all_reduce(est, op=torch.distributed.ReduceOp.MAX)
+    steps = int(min(max_steps, max(min_steps, budget_ms / float(est.item()))))
     flush = sum(t.numel() * t.element_size() for t in inputs) < 2 * L2_BYTES
-    total, per = time_steps(step, steps, flush, kdist.Rank(0, 1, rk.local_rank))
+    total, per = time_steps(step, steps, flush, world)
     ms = total / steps
     peak, src = roofline_peak(w)
     val = rate(w, ms)
     scale = 1e3 if w.bound == "hbm" else 1.0
-    del inputs
-    torch.cuda.empty_cache()
-    return {"value": round(val, 4), "unit": unit_of(w), "ms": round(ms, 5),
-            "ms_median": round(statistics.median(per), 5), "steps": steps,
-            "frac_of_peak": round(val * scale / peak, 4), "peak_source": src}
+    row = {"value": round(val, 4), "unit": unit_of(w), "ms": round(ms, 5),
+           "ms_median_rank0": round(statistics.median(per), 5), "steps": steps,
+           "frac_of_peak": round(val * scale / (peak * world), 4),
+           "peak": f"{world} x {peak} ({src})",
+           "per_rank": list(kdist.local_shape(w.kernel, w.shape, rk.rank, world)),
+           "launches": launches_per_call(local_workload(w, rk.rank, world)) * steps}
+    out = step()
+    torch.cuda.synchronize()
+    if rk.rank == 0:
+        row["check"] = rounded(spot_check(w, inputs, out), 8)
+    del out
+    if with_host:
+        e2e = time_e2e(w, inputs, steps=3, world=world, exchange=exchange)
+        row["e2e"] = rounded({k: v for k, v in e2e.items()}, 5)
+        del inputs, step
+        torch.cuda.empty_cache()
+        row["cpu_baseline"] = rounded(time_cpu(w, reps=5, budget_s=4.0), 5)
+    if isinstance(exchange, kdist.PeerSum):
+        exchange.close()
+    return row
 
+
+# ------------------------------------------------------------------ main
 
 def main() -> int:
     ap = argparse.ArgumentParser()
@@ -399,8 +467,10 @@ def main() -> int:
     ap.add_argument("--workload", choices=sorted(CONFIGS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-configs", action="store_true",
-                    help="skip the device-side table of the other headline workloads")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+                    help="skip the table of the other headline workloads")
+    ap.add_argument("--configs", default="",
+                    help="comma-separated workload keys for the table (default: all)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     ap.add_argument("--subset", type=int, default=0,
                     help="run a smaller instance: this many rows (softmax), rows of A (matmul), "
                          "batches (attention) or elements (reduce_sum); for profiling")
@@ -421,60 +491,84 @@ def main() -> int:
     w = CONFIGS[args.workload]
     if args.subset:
         w = subset_workload(w, args.subset)
-    inputs = w.inputs("cuda", seed=rk.rank)
+    lw = local_workload(w, rk.rank, rk.world)
+    inputs = kdist.shard_inputs(w.kernel, w.inputs("cuda", seed=0), rk.rank, rk.world)
+    torch.cuda.empty_cache()
     in_bytes = sum(t.numel() * t.element_size() for t in inputs)
     flush = in_bytes < 2 * L2_BYTES
-    exchange, exchange_desc = (reduce_exchange(rk) if w.kernel == "reduce_sum" and rk.world > 1
-                               else (None, "all_reduce(SUM) of fp32 partials"))
-    step = make_step(w, inputs, rk, exchange)
+    exchange, exchange_desc = (None, "none")
+    if w.kernel == "reduce_sum":
+        exchange, exchange_desc = (reduce_exchange(rk) if rk.world > 1
+                                   else (None, "none (one GPU)"))
+    step = make_step(w, inputs, exchange)
 
     with ClockSampler(physical_gpu_index(rk.local_rank)) as clocks:
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
-        total_ms, per = time_steps(step, args.steps, flush, rk)
+        total_ms, per = time_steps(step, args.steps, flush, rk.world)
     ms = total_ms / args.steps
+
+    check = None
     if w.kernel == "reduce_sum":
-        # one more call on every rank, outside the timing: the sum must be finite and no
-        # bounded wait (the peer exchange) may have given up during the run
+        # one more call on every rank, outside the timing, against the float64 sum of
+        # the global vector; no bounded wait (the peer exchange) may have given up
         import ctypes
 
-        check = float(step())
+        got = step().reshape(()).to(torch.float64)
+        ref = inputs[0].double().sum().reshape(1)
+        lo_hi = torch.stack([got, -got]).reshape(2)
+        if rk.world > 1:
+            torch.distributed.all_reduce(ref, op=torch.distributed.ReduceOp.SUM)
+            torch.distributed.all_reduce(lo_hi, op=torch.distributed.ReduceOp.MAX)
         word = ctypes.c_uint(0)
         ext.capi_check(ext.capi().kpb_device_errors(ctypes.byref(word)))
-        if not math.isfinite(check) or word.value:
-            raise RuntimeError(f"reduce_sum run invalid: result {check}, device error bits "
-                               f"{word.value:#x}")
-    value = rate(w, ms) * rk.world
+        tol = w.spec.tolerance(w.shape, w.dtype)
+        g, r = float(got), float(ref)
+        err = abs(g - r)
+        ok = (math.isfinite(g) and err <= tol.atol + tol.rtol * abs(r) and not word.value
+              and float(lo_hi[0]) == -float(lo_hi[1]))
+        check = {"result": g, "reference_f64": r, "max_abs_err": err, "atol": tol.atol,
+                 "rtol": tol.rtol, "same_bits_on_every_rank": float(lo_hi[0]) == -float(lo_hi[1]),
+                 "device_error_bits": word.value, "ok": ok}
+        if not ok:
+            raise RuntimeError(f"reduce_sum run invalid: {check}")
+
+    value = rate(w, ms)
     peak, peak_src = roofline_peak(w)
-    # dominant kernel: the op's own launches, timed per call on the op's stream
     local_ms = statistics.mean(per)
     step_stats = {"mean": round(local_ms, 5), "median": round(statistics.median(per), 5),
                   "min": round(min(per), 5), "max": round(max(per), 5)}
-    achieved = work_per_call(w) / (local_ms / 1e3) / (1e9 if w.bound == "hbm" else 1e12)
+    achieved = work_per_call(lw) / (local_ms / 1e3) / (1e9 if w.bound == "hbm" else 1e12)
     roof = {"bound": w.bound, "achieved": round(achieved, 2), "peak": peak,
             "unit": "GB/s" if w.bound == "hbm" else "TFLOP/s",
             "frac": round(achieved / peak, 4), "traffic": profiled_traffic(w),
-            "peak_source": f"{peak_src} (MEASURED_PEAKS.json)" if peak_src == "measured"
-            else "fallback"}
+            "peak_source": f"{peak_src} (MEASURED_PEAKS.json)" if peak_src != "fallback"
+            else "fallback",
+            "kernel": "rank 0's call on its shard, mean device time per call"}
 
-    e2e = time_e2e(w, inputs, args.e2e_steps, rk, exchange) if args.e2e_steps > 0 else None
+    e2e = time_e2e(w, inputs, args.e2e_steps, rk.world, exchange) if args.e2e_steps > 0 else None
 
     configs = {}
     configs_clocks = None
-    if rk.world == 1 and not args.no_configs:
+    if not args.no_configs:
         del inputs, step
         torch.cuda.empty_cache()
+        keys = [k for k in (args.configs.split(",") if args.configs else CONFIGS) if k]
+        with_host = rk.world == 1 and not args.no_cpu
         # clocks sampled over the whole table too: its numbers are only comparable
         # between runs at the same clocks
         with ClockSampler(physical_gpu_index(rk.local_rank)) as table_clocks:
-            for key, other in CONFIGS.items():
+            for key in keys:
                 if key == w.key:
                     continue
                 try:
-                    configs[key] = quick_measure(other, rk)
+                    configs[key] = measure_row(CONFIGS[key], rk, with_host)
                 except Exception as e:  # reported in the line, never hidden
                     configs[key] = {"error": f"{type(e).__name__}: {e}"[:300]}
+                    if rk.world > 1:
+                        raise  # the ranks would go out of step
+                torch.cuda.empty_cache()
         configs_clocks = table_clocks.summary()
 
     cpu = None
@@ -482,35 +576,35 @@ def main() -> int:
         cpu = time_cpu(w, reps=5)
 
     if rk.world > 1:
-        torch.distributed.barrier()
         torch.cuda.synchronize()
+        torch.distributed.barrier()
         if isinstance(exchange, kdist.PeerSum):
-            torch.distributed.barrier()  # no rank still writes into a peer's buffer
-            exchange.close()
+            exchange.close()  # collective: synchronises and waits for every rank
         torch.distributed.destroy_process_group()
     if rk.rank != 0:
         return 0
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": unit_of(w), "n_gpus": rk.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-        "step_ms": step_stats,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": DTYPE_NAMES[w.dtype], "data": "synthetic",
-        "config": {"workload": w.key, "shape": list(w.shape), "description": w.description,
-                   "per_rank": "one full instance per GPU",
-                   "l2": "flushed between steps outside the events (256 MB written, then read so no dirty lines remain)" if flush else "inputs larger than L2",
-                   "exchange": (exchange_desc if rk.world > 1 else "none (one GPU)")
-                   if w.kernel == "reduce_sum" else "none", "parallelism": f"dp{rk.world}"},
+        "step_ms_rank0": step_stats,
+        "higher_is_better": True, "scaling": "strong" if rk.world > 1 else "weak",
+        "vs_baseline": None, "dtype": DTYPE_NAMES[w.dtype], "data": "synthetic",
+        "config": job_config(w, rk.world),
+        "timing": {"l2": "flushed between steps outside the events (256 MB written, then "
+                         "read so no dirty lines remain)" if flush else
+                   "each rank's inputs larger than twice the L2",
+                   "exchange": exchange_desc,
+                   "ranks": "max over ranks of the summed per-step CUDA-event times"},
         "pct_of_peak": round(value * (1e3 if w.bound == "hbm" else 1.0) / (peak * rk.world), 4),
         "roofline": roof,
-        "e2e": ({k: (round(v, 5) if isinstance(v, float) else v) for k, v in e2e.items()}
-                if e2e else None),
-        "gpu_launches": launches_per_call(w) * args.steps,
+        "e2e": rounded(e2e) if e2e else None,
+        "gpu_launches": launches_per_call(lw) * args.steps,
         "clocks": clocks.summary(),
     }
+    if check:
+        line["check"] = check
     if cpu:
-        line["cpu_baseline"] = {k: (round(v, 5) if isinstance(v, float) else v)
-                                for k, v in cpu.items()}
+        line["cpu_baseline"] = rounded(cpu)
     if configs:
         line["configs"] = configs
         line["configs_clocks"] = configs_clocks

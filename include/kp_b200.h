@@ -91,14 +91,20 @@ int kpb_reduce_sum_noalloc(int dtype, const void* x, float* out, int64_t n, void
  * kpb_peer_sum_create exports this rank's small exchange buffer as a CUDA IPC handle
  * (kpb_peer_sum_handle_bytes() bytes); the caller gathers every rank's handle in rank
  * order (any host-side all_gather) and passes them to kpb_peer_sum_connect. Then every
- * rank calls kpb_peer_sum_run the same number of times, in the same order: each call
- * reduces the local shard (the persistent kernel; partials in the caller's workspace
- * of kpb_peer_sum_workspace_bytes(n) bytes) and its one-CTA finishing kernel stores
- * the local sum into every rank's buffer over NVLink, waits (bounded) for the other
- * ranks' sums and writes out[0] = sum over ranks in rank order: the same bits on every
- * rank. A rank that never arrives makes the others set the timeout bit of
- * kpb_device_errors() and write NaN. At most 8 ranks; all on one node with
- * peer access (NVLink/NVSwitch). */
+ * rank calls kpb_peer_sum_run the same number of times, in the same order, all calls
+ * of a rank on one stream: each call reduces the local shard (the persistent kernel;
+ * partials in the caller's workspace of kpb_peer_sum_workspace_bytes(n) bytes) and
+ * its one-CTA finishing kernel stores the local sum into every rank's buffer over
+ * NVLink, waits (bounded) for the other ranks' sums and writes out[0] = sum over
+ * ranks in rank order: the same bits on every rank. The call number is kept in device
+ * memory and advanced by the kernel, so a CUDA graph holding the call can be replayed
+ * (every rank replaying the same number of times). A rank that never arrives makes
+ * the others set the timeout bit of kpb_device_errors(), write NaN and mark their
+ * exchange out of step; from then on every call writes NaN at once.
+ * kpb_peer_sum_status (synchronous) reports that mark. Call kpb_peer_sum_destroy only
+ * once every rank's calls have completed (a device synchronise and a barrier across
+ * the ranks), since the peers store into this rank's buffer. At most 8 ranks; all on
+ * one node with peer access (NVLink/NVSwitch). */
 typedef struct kpb_peer_sum kpb_peer_sum;
 size_t kpb_peer_sum_handle_bytes(void);
 int kpb_peer_sum_create(int rank, int world, void* ipc_handle_out, kpb_peer_sum** out);
@@ -106,6 +112,7 @@ int kpb_peer_sum_connect(kpb_peer_sum* ps, const void* all_handles);
 size_t kpb_peer_sum_workspace_bytes(int64_t n);
 int kpb_peer_sum_run(kpb_peer_sum* ps, int dtype, const void* x, float* out, int64_t n,
                      void* workspace, size_t workspace_bytes, void* stream);
+int kpb_peer_sum_status(kpb_peer_sum* ps, int* out_of_step);
 int kpb_peer_sum_destroy(kpb_peer_sum* ps);
 
 /* ---- row softmax: replaces kp::softmax (csrc/launchers.h:17-18) ----

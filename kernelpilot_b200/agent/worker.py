@@ -11,9 +11,10 @@ csrc/compat.h), into the candidate's own build directory. Then, in order:
 
 1. compile      a compiler error ends the evaluation (stage "compile");
 2. correctness  every test shape of the op's spec against the float64 reference, with
-                the spec's tolerances (``correctness.check_impl``);
+                the spec's tolerances (the reference harness's ``check_impl``);
 3. benchmark    every benchmark shape, re-verified, timed against the PyTorch built-in
-                the spec names as its baseline (``benchmark.bench_one``);
+                the spec names as its baseline (the reference harness's ``bench_one``,
+                with the B200 peaks of ``harness.gpu_info``);
 4. profile      the kernels one call launches (torch.profiler) and, from ptxas, each
                 kernel's registers, spills and static shared memory.
 
@@ -154,10 +155,11 @@ def evaluate(kernel: str, lang: str, dtype_name: str, code_path: Path, build_dir
              bench_shapes: list[tuple] | None = None) -> EvalResult:
     import torch
 
-    from ..benchmark import bench_one
-    from ..correctness import check_impl
-    from ..device import get_gpu_info
+    from .. import harness
     from ..specs import get_spec
+
+    check_impl = harness.check_impl
+    bench_one = harness.reference().benchmark.bench_one
 
     t0 = time.monotonic()
 
@@ -195,7 +197,7 @@ def evaluate(kernel: str, lang: str, dtype_name: str, code_path: Path, build_dir
         passed += 1
 
     # 3. benchmark against the PyTorch built-in, every shape verified again
-    gpu = get_gpu_info()
+    gpu = harness.gpu_info()
     rows = []
     try:
         for shape in bench_shapes or spec.bench_shapes:
@@ -230,7 +232,9 @@ def main(argv: list[str] | None = None) -> int:
     p.add_argument("--lang", choices=LANGS, default="cuda")
     p.add_argument("--dtype", default="float32")
     p.add_argument("--code", required=True)
-    p.add_argument("--out", required=True)
+    dest = p.add_mutually_exclusive_group(required=True)
+    dest.add_argument("--out", help="write the result JSON to this file")
+    dest.add_argument("--result-fd", type=int, help="write the result JSON to this open fd")
     p.add_argument("--build-dir", default=None)
     p.add_argument("--bench-shapes", default=None, help="JSON list of shapes")
     a = p.parse_args(argv)
@@ -241,7 +245,12 @@ def main(argv: list[str] | None = None) -> int:
         res = evaluate(a.kernel, a.lang, a.dtype, code, build, shapes)
     except Exception:
         res = EvalResult(stage="crash", error=_tail(traceback.format_exc()))
-    Path(a.out).write_text(json.dumps(res.to_dict()))
+    payload = json.dumps(res.to_dict())
+    if a.out:
+        Path(a.out).write_text(payload)
+    else:
+        with os.fdopen(a.result_fd, "w") as f:
+            f.write(payload)
     return 0
 
 

@@ -6,22 +6,30 @@
 // on one GPU (csrc/kernels/reduction.hip:86). The data-parallel layer here shards
 // the vector and needs one exchange step: the sum of the per-GPU partials. Done as
 // an NCCL all_reduce of one float that step costs a separate kernel and ~10-15 us of
-// collective latency per call, about 8% of the 150 us per-GPU reduction of 2^28
-// values. Here the one-CTA finishing kernel of the persistent reduction does it:
-//   * every rank owns an exchange buffer of 2 x 8 words (cudaMalloc'd once, exported
-//     as a CUDA IPC handle; every rank opens the others' handles once);
-//   * call k (a counter every rank advances in step) uses row k & 1 of the buffers:
-//     the kernel adds its local partials in a fixed order, then stores the word
-//     (k << 32 | bits of its sum) into slot [k & 1][rank] of every rank's buffer
-//     (a system-scope release store, over NVLink for the peers), then one thread per
-//     rank polls its own buffer's slot [k & 1][r] until the word carries k, and the
-//     sums are added in rank order. Every rank therefore computes the same value,
-//     bit for bit, whatever the timing.
-//   * Two rows suffice: a rank can only start call k + 2 (reusing row k & 1) after it
+// collective latency per call. Here the one-CTA finishing kernel of the persistent
+// reduction does it:
+//   * every rank owns an exchange buffer (cudaMalloc'd once, exported as a CUDA IPC
+//     handle; every rank opens the others' handles once) holding 2 rows x 8 slots of
+//     64-bit words that peers write, and two control words only its own rank uses:
+//     the call counter and a sticky "out of step" flag;
+//   * the call number k lives in device memory: each finishing kernel reads the
+//     counter, uses k = counter + 1 and writes k back. Calls are ordered on one
+//     stream, so a CUDA graph that captured the call advances k on every replay just
+//     as eager calls do;
+//   * call k uses row k & 1: the kernel adds its local partials in a fixed order, then
+//     stores the word (k << 32 | bits of its sum) into slot [k & 1][rank] of every
+//     rank's buffer (a system-scope release store, over NVLink for the peers), then
+//     one thread per rank polls its own buffer's slot [k & 1][r] until the word
+//     carries k, and the sums are added in rank order. Every rank therefore computes
+//     the same value, bit for bit, whatever the timing;
+//   * two rows suffice: a rank can only start call k + 2 (reusing row k & 1) after it
 //     has read every rank's call-(k + 1) word, which each rank writes only after it
-//     has read its call-k words.
-//   * Each poll is bounded (kWaitLimitNs): a rank that never arrives makes the others
-//     set kErrTimeout in the device error word and write NaN, instead of spinning.
+//     has read its call-k words;
+//   * each poll is bounded (kWaitLimitNs): a rank that never arrives makes the others
+//     set kErrTimeout in the device error word, write NaN and set the sticky flag.
+//     Once the flag is set the ranks are out of step for good, so every later call
+//     writes NaN and sets kErrTimeout at once instead of waiting again;
+//     kpb_peer_sum_status reads the flag.
 // There are no multicast loads and no memory of another GPU is given to TMA.
 #include <cstring>
 
@@ -39,7 +47,11 @@ namespace {
 
 constexpr int kPeerMax = 8;                      // GPUs of one node
 constexpr int kPeerFinishThreads = 1024;
-constexpr size_t kExchangeBytes = 2 * kPeerMax * sizeof(unsigned long long);
+// words 0 .. 2*kPeerMax-1: the two exchange rows; then the local control words
+constexpr int kCtlSeq = 2 * kPeerMax;            // last call number this rank ran
+constexpr int kCtlBroken = 2 * kPeerMax + 1;     // non-zero once a wait gave up
+constexpr size_t kExchangeBytes = 32 * sizeof(unsigned long long);
+static_assert(kCtlBroken < 32, "control words fit the exchange buffer");
 
 struct PeerSlots {
   unsigned long long* buf[kPeerMax];             // each rank's exchange buffer, mapped here
@@ -56,15 +68,35 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
 
 __global__ void __launch_bounds__(kPeerFinishThreads)
 sum_finish_peers(const float* __restrict__ partials, int64_t count, float* __restrict__ out,
-                 PeerSlots slots, int rank, int world, unsigned seq, unsigned* err) {
+                 PeerSlots slots, int rank, int world, unsigned* err) {
   __shared__ float scratch[kWarp];
   __shared__ float vals[kPeerMax];
   __shared__ int all_ok;
+  __shared__ unsigned call;
+  __shared__ int broken;
   pdl_wait_primary();
+  unsigned long long* own = slots.buf[rank];
+  if (threadIdx.x == 0) {
+    // only this rank's finishing kernels touch its control words, one after the
+    // other in stream order, so plain accesses suffice
+    unsigned k = static_cast<unsigned>(own[kCtlSeq]) + 1u;
+    if (k == 0) k = 1;  // 0 marks a slot never written
+    own[kCtlSeq] = k;
+    call = k;
+    broken = own[kCtlBroken] != 0;
+    all_ok = 1;
+  }
   float s = 0.f;
   for (int64_t i = threadIdx.x; i < count; i += kPeerFinishThreads) s += partials[i];
-  s = block_reduce<false>(s, scratch);  // every thread holds the CTA sum
-  if (threadIdx.x == 0) all_ok = 1;
+  s = block_reduce<false>(s, scratch);  // every thread holds the CTA sum (and sees call)
+  const unsigned seq = call;
+  if (broken) {
+    if (threadIdx.x == 0) {
+      atomicOr(err, kErrTimeout);
+      out[0] = __int_as_float(0x7fc00000);
+    }
+    return;
+  }
   const int row = static_cast<int>(seq & 1u) * kPeerMax;
   const unsigned long long word =
       (static_cast<unsigned long long>(seq) << 32) | __float_as_uint(s);
@@ -73,7 +105,7 @@ sum_finish_peers(const float* __restrict__ partials, int64_t count, float* __res
   __syncthreads();
   // collect every rank's partial of this call from the own buffer
   if (threadIdx.x < world) {
-    const unsigned long long* slot = slots.buf[rank] + row + threadIdx.x;
+    const unsigned long long* slot = own + row + threadIdx.x;
     unsigned long long v = ld_acquire_sys_u64(slot);
     if (static_cast<unsigned>(v >> 32) != seq) {
       const uint64_t t0 = global_timer_ns();
@@ -96,6 +128,7 @@ sum_finish_peers(const float* __restrict__ partials, int64_t count, float* __res
     float total = 0.f;
     for (int r = 0; r < world; ++r) total += vals[r];  // rank order: the same on every rank
     out[0] = all_ok ? total : __int_as_float(0x7fc00000);
+    if (!all_ok) own[kCtlBroken] = 1;
   }
 }
 
@@ -108,7 +141,6 @@ struct kpb_peer_sum {
   unsigned long long* peer[kpb::kPeerMax] = {};
   bool opened[kpb::kPeerMax] = {};
   bool connected = false;
-  unsigned seq = 0;
 };
 
 extern "C" {
@@ -196,7 +228,6 @@ int kpb_peer_sum_run(kpb_peer_sum* ps, int dtype, const void* x, float* out, int
   if (n > 0) {
     if (int rc = reduce_level1_persistent(dtype, x, n, partials, &ctas, s)) return rc;
   }
-  if (++ps->seq == 0) ps->seq = 1;  // 0 marks a slot never written
   PeerSlots slots{};
   for (int r = 0; r < ps->world; ++r) slots.buf[r] = ps->peer[r];
   cudaLaunchConfig_t cfg = {};
@@ -209,7 +240,23 @@ int kpb_peer_sum_run(kpb_peer_sum* ps, int dtype, const void* x, float* out, int
   cfg.attrs = attr;
   cfg.numAttrs = n > 0 ? 1 : 0;
   KPB_CUDA(cudaLaunchKernelEx(&cfg, sum_finish_peers, static_cast<const float*>(partials), ctas,
-                              out, slots, ps->rank, ps->world, ps->seq, err));
+                              out, slots, ps->rank, ps->world, err));
+  return KPB_OK;
+}
+
+int kpb_peer_sum_status(kpb_peer_sum* ps, int* out_of_step) {
+  using namespace kpb;
+  set_error("");
+  if (ps == nullptr || out_of_step == nullptr)
+    return fail(KPB_EINVAL, "peer_sum_status: null pointer");
+  int dev = -1;
+  KPB_CUDA(cudaGetDevice(&dev));
+  if (dev != ps->device)
+    return fail(KPB_EINVAL, "peer_sum_status: current device differs from the one it was created on");
+  unsigned long long flag = 0;
+  KPB_CUDA(cudaDeviceSynchronize());
+  KPB_CUDA(cudaMemcpy(&flag, ps->local + kCtlBroken, sizeof(flag), cudaMemcpyDeviceToHost));
+  *out_of_step = flag != 0;
   return KPB_OK;
 }
 

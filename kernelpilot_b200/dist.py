@@ -68,6 +68,55 @@ def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
     return start, start + base + (1 if rank < extra else 0)
 
 
+# the axis each op is split along, and what a rank holds
+PARTITION: dict[str, str] = {
+    "reduce_sum": "contiguous element chunks (sizes differ by at most one)",
+    "vector_add": "contiguous element chunks of a and b",
+    "softmax": "row blocks",
+    "layernorm": "row blocks (w and b replicated)",
+    "matmul": "M-blocks: row blocks of A and C (B replicated)",
+    "attention": "(batch, head) slices of q, k, v and o",
+    "attention_causal": "(batch, head) slices of q, k, v and o",
+}
+
+
+def _units(kernel: str, shape: tuple) -> int:
+    """Independent units of an op's shape along its partition axis."""
+    if kernel in ("attention", "attention_causal"):
+        return shape[0] * shape[1]
+    return shape[0]
+
+
+def local_shape(kernel: str, shape: tuple, rank: int, world: int) -> tuple:
+    """The shape this rank's shard of a global ``shape`` has, as the op sees it."""
+    if kernel not in PARTITION:
+        raise KeyError(f"no partition for {kernel!r}")
+    if world == 1:
+        return tuple(shape)
+    a, b = shard_range(_units(kernel, shape), rank, world)
+    if kernel in ("attention", "attention_causal"):
+        return (1, b - a) + tuple(shape[2:])
+    return (b - a,) + tuple(shape[1:])
+
+
+def shard_inputs(kernel: str, inputs: tuple, rank: int, world: int) -> tuple:
+    """This rank's part of the global inputs, as contiguous tensors (copies when
+    world > 1, so the global tensors can be freed)."""
+    if world == 1:
+        return tuple(inputs)
+    if kernel in ("attention", "attention_causal"):
+        B, H, S, D = inputs[0].shape
+        a, b = shard_range(B * H, rank, world)
+        return tuple(t.reshape(B * H, S, D)[a:b].reshape(1, b - a, S, D).clone()
+                     for t in inputs)
+    a, b = shard_range(_units(kernel, tuple(inputs[0].shape)), rank, world)
+    if kernel in ("reduce_sum", "vector_add"):
+        return tuple(t.reshape(-1)[a:b].clone() for t in inputs)
+    if kernel in ("softmax", "matmul", "layernorm"):
+        return (inputs[0][a:b].clone(),) + tuple(inputs[1:])
+    raise KeyError(f"no partition for {kernel!r}")
+
+
 def sharded_reduce_sum(x_local: torch.Tensor, op: Callable[[torch.Tensor], torch.Tensor]
                        ) -> torch.Tensor:
     """Global sum: the local fp32 partial of this rank's chunk, combined by one
@@ -89,15 +138,25 @@ class PeerSum:
     the same order as its other collectives): the ranks export their exchange buffers
     as CUDA IPC handles, agree that all exports worked (else every rank raises and the
     caller can fall back to ``sharded_reduce_sum``) and all-gather the handles. Calls
-    must then be made by every rank, the same number of times, in the same order.
+    must then be made by every rank, the same number of times, in the same order, on
+    one stream per rank. The call number lives in device memory, so a call captured in
+    a CUDA graph may be replayed (by every rank, equally often).
+
+    If a rank misses a call, the others' bounded waits give up: they return NaN and
+    their exchange is marked out of step for good (later calls return NaN at once).
+    ``healthy()`` (collective, synchronising) finds that out; after it has returned
+    False every call raises, and the caller can fall back to ``sharded_reduce_sum``.
     """
 
     def __init__(self, group=None):
         from . import ext
 
         self._lib = lib = ext.capi()
+        self._group = group
+        self._broken = False
         world = dist.get_world_size(group) if dist.is_initialized() else 1
         rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self._world = world
         nb = lib.kpb_peer_sum_handle_bytes()
         handle = ctypes.create_string_buffer(nb)
         self._ps = ctypes.c_void_p()
@@ -109,7 +168,7 @@ class PeerSum:
             ok = torch.tensor([1 if rc == 0 else 0], device=dev)
             dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
             if int(ok.item()) == 0:
-                self.close()
+                self._release()
                 raise RuntimeError(f"peer sum unavailable on some rank ({msg or 'another rank'})")
             mine = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).to(dev)
             every = torch.empty(world * nb, dtype=torch.uint8, device=dev)
@@ -128,13 +187,18 @@ class PeerSum:
             dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
             rc = 0 if int(ok.item()) == 1 else (rc or 1)
         if rc:
-            self.close()
+            self._release()
             raise RuntimeError(f"peer sum connect failed on some rank ({msg or 'another rank'})")
         self._ws = torch.empty(0, dtype=torch.uint8, device=dev)
 
     def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
         from . import ext
 
+        if self._broken:
+            raise RuntimeError("peer sum is out of step (a rank missed a call); "
+                               "use sharded_reduce_sum")
+        if self._ps is None:
+            raise RuntimeError("peer sum is closed")
         x = x_local.reshape(-1)
         if not x.is_contiguous():
             x = x.contiguous()
@@ -148,9 +212,35 @@ class PeerSum:
             self._ws.data_ptr(), self._ws.numel(), ext.current_stream_ptr(x.device)))
         return out
 
+    def healthy(self) -> bool:
+        """True while every rank's exchange is in step. Collective at world > 1 (every
+        rank must call it, at the same point of its call sequence); synchronises the
+        device. Once False, later calls raise."""
+        from . import ext
+
+        if self._ps is None:
+            return False
+        flag = ctypes.c_int(0)
+        ext.capi_check(self._lib.kpb_peer_sum_status(self._ps, ctypes.byref(flag)))
+        bad = torch.tensor([flag.value], device=self._ws.device, dtype=torch.int32)
+        if self._world > 1:
+            dist.all_reduce(bad, op=dist.ReduceOp.MAX, group=self._group)
+        if int(bad.item()):
+            self._broken = True
+        return not self._broken
+
     def close(self) -> None:
-        """Release the exchange buffer and the peers' mappings (after a barrier, so no
-        rank still writes into them)."""
+        """Release the exchange buffer and the peers' mappings. Collective at world > 1:
+        each rank waits for its own work to finish, then for every other rank to get
+        here, so no peer still stores into a buffer that is being freed."""
+        if getattr(self, "_ps", None) is None:
+            return
+        if self._world > 1 and dist.is_initialized():
+            torch.cuda.synchronize()
+            dist.barrier(group=self._group)
+        self._release()
+
+    def _release(self) -> None:
         if getattr(self, "_ps", None) is not None and self._ps.value:
             self._lib.kpb_peer_sum_destroy(self._ps)
         self._ps = None

@@ -74,6 +74,7 @@ CAPI_SIGNATURES: dict[str, tuple] = {
     "kpb_peer_sum_connect": (_i32, [_vp, _vp]),
     "kpb_peer_sum_workspace_bytes": (_sz, [_i64]),
     "kpb_peer_sum_run": (_i32, [_vp, _i32, _vp, _vp, _i64, _vp, _sz, _vp]),
+    "kpb_peer_sum_status": (_i32, [_vp, ctypes.POINTER(_i32)]),
     "kpb_peer_sum_destroy": (_i32, [_vp]),
     "kpb_softmax": (_i32, [_i32, _i32, _vp, _vp, _i64, _i64, _vp]),
     "kpb_matmul": (_i32, [_i32, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),

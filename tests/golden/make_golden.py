@@ -1,9 +1,9 @@
 """Generates the golden fixtures in this directory from the reference itself.
 
-Run once, in a checkout that has the reference package available (its path is the
-first argument, default /root/reference):
+Run once, in a checkout that has the reference package available (the path of the
+kernelpilot source tree is the first, required, argument):
 
-    python tests/golden/make_golden.py [/path/to/kernelpilot] [op ...]
+    python tests/golden/make_golden.py /path/to/kernelpilot [op ...]
 
 For every op, dtype and shape below it calls the reference's own input generator
 (``spec.make_inputs(shape, dtype, cpu, seed=0)``, kernelpilot/specs.py:69-72) and its
@@ -75,4 +75,6 @@ def main(ref_root: str, ops: list[str]) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2:])
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/kernelpilot [op ...]")
+    main(sys.argv[1], sys.argv[2:])

@@ -49,3 +49,19 @@ def test_work_per_call_is_the_spec_formula():
     # causal: the useful FLOPs (half the scores plus the diagonal)
     assert bench.work_per_call(CONFIGS["attn_causal_bf16_b8h32s4096d128"]) == pytest.approx(
         4 * 8 * 32 * 4096 * 4097 / 2 * 128)
+
+
+@pytest.mark.parametrize("world", [1, 2, 8])
+def test_both_arms_print_the_same_config(world):
+    for key, w in CONFIGS.items():
+        cfg = bench.job_config(w, world)
+        assert cfg == bench.job_config(w, world)
+        assert cfg["workload"] == key and cfg["parallelism"] == f"dp{world}"
+        # a rank's shard is one of the listed shapes
+        assert list(bench.local_workload(w, world - 1, world).shape) in cfg["per_rank"]
+
+
+def test_partitioned_reduction_shards_are_near_equal():
+    w = CONFIGS["reduce_f32_2p28p1"]
+    sizes = [bench.local_workload(w, r, 8).shape[0] for r in range(8)]
+    assert sum(sizes) == 2**28 + 1 and max(sizes) - min(sizes) == 1

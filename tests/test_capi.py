@@ -89,7 +89,8 @@ def test_workspace_queries(lib):
 def test_ctypes_types_are_plain():
     # the boundary has no torch types: every argument is an int, a float, a size or a pointer
     allowed = {ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_float,
-               ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_void_p)}
+               ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_void_p),
+               ctypes.POINTER(ctypes.c_int)}
     for _name, (_res, args) in ext.CAPI_SIGNATURES.items():
         assert all(a in allowed for a in args)
 
@@ -108,3 +109,9 @@ def test_peer_sum_rejects_bad_arguments_without_a_gpu(lib):
     assert lib.kpb_peer_sum_destroy(None) == 0
     assert lib.kpb_peer_sum_workspace_bytes(0) == 0
     assert lib.kpb_peer_sum_workspace_bytes(1 << 20) >= 4
+
+
+def test_peer_sum_status_rejects_null_without_a_gpu(lib):
+    flag = ctypes.c_int(7)
+    assert lib.kpb_peer_sum_status(None, ctypes.byref(flag)) == 1
+    assert b"null" in lib.kpb_last_error()

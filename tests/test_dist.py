@@ -104,3 +104,79 @@ def test_peer_sum_unavailable_on_every_rank_falls_back_together():
     for rank, outcome, total in results:
         assert outcome.startswith("peer sum unavailable"), (rank, outcome, total)
         assert total == 30.0  # 10 * 1 + 10 * 2 on both ranks, through the fallback
+
+
+@pytest.mark.parametrize("kernel,shape", [
+    ("reduce_sum", (1001,)), ("vector_add", (17,)), ("softmax", (7, 5)), ("layernorm", (9, 4)),
+    ("matmul", (10, 3, 4)), ("attention", (2, 3, 8, 4)), ("attention_causal", (1, 5, 8, 4))])
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_shards_reassemble_the_global_inputs(kernel, shape, world):
+    from kernelpilot_b200.specs import get_spec
+
+    spec = get_spec(kernel)
+    full = spec.make_inputs(shape, torch.float32, torch.device("cpu"), 0)
+    parts = [kdist.shard_inputs(kernel, full, r, world) for r in range(world)]
+    for r, p in enumerate(parts):
+        # matmul's spec shape is (M, N, K): A is (M, K), B is (K, N)
+        seen = (p[0].shape[0], p[1].shape[1], p[0].shape[1]) if kernel == "matmul" \
+            else tuple(p[0].shape)
+        assert seen == kdist.local_shape(kernel, shape, r, world)
+        assert all(t.is_contiguous() for t in p)
+    if kernel in ("attention", "attention_causal"):
+        B, H, S, D = shape
+        for i in range(3):
+            got = torch.cat([p[i].reshape(-1, S, D) for p in parts]).reshape(shape)
+            assert torch.equal(got, full[i])
+    elif kernel in ("reduce_sum", "vector_add"):
+        for i in range(len(full)):
+            assert torch.equal(torch.cat([p[i] for p in parts]), full[i])
+    else:
+        assert torch.equal(torch.cat([p[0] for p in parts]), full[0])
+        for i in range(1, len(full)):  # replicated operands
+            assert all(torch.equal(p[i], full[i]) for p in parts)
+    # the shards' work adds up to the job's (up to the reduction's 4-byte result each)
+    if kernel != "reduce_sum":
+        total = sum(spec.flops(kdist.local_shape(kernel, shape, r, world)) for r in range(world))
+        assert total == pytest.approx(spec.flops(shape)) or kernel == "attention_causal"
+
+
+def _sharded_op_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    try:
+        from kernelpilot_b200.specs import get_spec
+
+        kdist.init(backend="gloo", timeout_s=30)
+        ok = []
+        for kernel, shape in [("softmax", (9, 33)), ("matmul", (9, 5, 7)),
+                              ("attention", (1, 3, 16, 8)), ("layernorm", (5, 12))]:
+            spec = get_spec(kernel)
+            full = spec.make_inputs(shape, torch.float32, torch.device("cpu"), 0)
+            local = kdist.shard_inputs(kernel, full, rank, world)
+            out = spec.baseline(*local)
+            if kernel == "attention":
+                B, H, S, D = shape
+                counts = kdist.row_counts(B * H, world)
+                got = kdist.assemble_rows(out.reshape(-1, S, D).contiguous(), counts)
+                got = got.reshape(shape)
+            else:
+                got = kdist.assemble_rows(out.contiguous(), kdist.row_counts(shape[0], world))
+            ok.append(bool(torch.allclose(got, spec.baseline(*full), atol=1e-5, rtol=1e-5)))
+        q.put((rank, ok))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+def test_two_gloo_ranks_split_each_op_and_reassemble_its_output():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_op_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok in results:
+        assert ok == [True, True, True, True], (rank, ok)

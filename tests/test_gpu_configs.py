@@ -10,7 +10,7 @@ import pytest
 import torch
 
 from kernelpilot_b200 import registry
-from kernelpilot_b200.correctness import check_chunked
+from kernelpilot_b200.harness import check_chunked
 from kernelpilot_b200.specs import CONFIGS
 
 pytestmark = pytest.mark.gpu

@@ -21,7 +21,7 @@ import pytest
 import torch
 
 from kernelpilot_b200 import ext, registry
-from kernelpilot_b200.correctness import check_impl, check_on_inputs, compare
+from kernelpilot_b200.harness import check_impl, check_on_inputs, compare
 from kernelpilot_b200.specs import SPECS, get_spec
 
 pytestmark = pytest.mark.gpu

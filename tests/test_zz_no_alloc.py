@@ -1,9 +1,11 @@
 """kpb_reduce_sum_noalloc, the full sum for callers that may not allocate device
 memory when they call (fixed start-up budgets, memory owned by another allocator,
 runtimes that forbid allocation after initialisation): called through the C ABI, its
-result must match the allocating entry point kpb_reduce_sum within the reduction's
-tolerance, on two calls in a row with different inputs (the built-in scratch keeps the
-previous call's partials, so a stale value would show up in the second call).
+result must be identical, bit for bit, to the allocating entry point kpb_reduce_sum's
+(both run the same kernels and add the partials in the same fixed order), on two calls
+in a row with different inputs: the built-in scratch keeps the previous call's
+partials, so a stale or overlapping partial would show up in the second call. The
+results are also within the reduction's tolerance of the float64 sum.
 
 This file sorts last so that a run stopping at the first failure has already run every
 other test; it also passes alone in a fresh process.
@@ -36,8 +38,9 @@ def test_noalloc_matches_allocating_entry_point_twice(dtype, n):
         ext.capi_check(lib.kpb_reduce_sum_noalloc(code, x.data_ptr(), got.data_ptr(), n,
                                                   stream))
         torch.cuda.synchronize()
-        w, g = float(want), float(got)
-        assert abs(g - w) <= tol.atol + tol.rtol * abs(w), (str(dtype), n, g, w)
+        assert torch.equal(got, want), (str(dtype), n, float(got), float(want))
+        exact = float(x.double().sum())
+        assert abs(float(got) - exact) <= tol.atol + tol.rtol * abs(exact)
 
 
 def test_noalloc_rejects_bad_arguments():
