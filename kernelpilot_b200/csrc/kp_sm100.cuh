@@ -127,6 +127,69 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int32_t
       : "memory");
 }
 
+// 2-D tiled load issued by either CTA of a CTA pair (cta_group::2): the data lands
+// in the issuing CTA's shared memory and the transaction bytes complete on the
+// mbarrier at `bar_cluster`, a shared::cluster address that may be the pair leader's.
+// Each CTA loads only its own tile; nothing is broadcast to the other CTA.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, int32_t x, int32_t y,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];"
+      :: "r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(bar_cluster) : "memory");
+}
+
+// Address of the same shared-memory object in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t cluster_map(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// Arrive once on an mbarrier given by its shared::cluster address (possibly in
+// another CTA of the cluster), with release semantics at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+               :: "r"(bar_cluster) : "memory");
+}
+
+// mbar_wait whose completion also acquires at cluster scope (the arrivals it waits
+// for came from another CTA of the cluster).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, unsigned* err) {
+  const uint32_t a = smem_u32(bar);
+  auto try_once = [&]() {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done) : "r"(a), "r"(parity) : "memory");
+    return done != 0;
+  };
+  if (try_once()) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (try_once()) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (err) atomicOr(err, kErrTimeout);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t cta_rank_in_cluster() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of both CTAs of the pair.
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
 }
@@ -144,6 +207,20 @@ __device__ __forceinline__ void tmem_relinquish() {
 }
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+               :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+// The same three operations for a CTA pair (cta_group::2): one warp of EACH CTA of
+// the pair executes them together; both pass the same shared-memory offset.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+               :: "r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;"
                :: "r"(taddr), "r"(ncols) : "memory");
 }
 
@@ -173,6 +250,27 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
       :: "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// CTA-pair MMA (issued by one thread of the pair's leader CTA): D (M = 256 rows, half
+// in each CTA's TMEM) (+)= A (128 rows from each CTA's shared memory, same offset)
+// * B (N/2 columns from each CTA's shared memory, same offset).
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// Arrive once on the mbarrier at `bar`'s offset in every CTA of `cta_mask` when every
+// tcgen05 operation the pair issued so far is done.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;"
+      :: "r"(smem_u32(bar)), "h"(cta_mask) : "memory");
 }
 
 // Arrive once on `bar` when every tcgen05 operation this thread issued so far is done.

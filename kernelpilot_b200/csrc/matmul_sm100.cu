@@ -19,6 +19,8 @@
 // Shapes TMA cannot describe (a row pitch that is not a multiple of 16 bytes, e.g.
 // N = 4097, or an unaligned base) are first copied into a zero-padded, aligned
 // workspace; C is written with masked stores, so any M, N, K works.
+#include <cstdlib>
+
 #include "kp_common.cuh"
 #include "kp_sm100.cuh"
 
@@ -123,6 +125,7 @@ gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtenso
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
+      pdl_wait_primary();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -239,6 +242,205 @@ gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtenso
   }
 }
 
+// ------------------------------------------------------------------ CTA-pair kernel
+//
+// The same roles on a cluster of two CTAs on two SMs (cta_group::2). A pair computes a
+// 256 x 256 tile: CTA r loads rows [128 r, 128 r + 128) of the A block and columns
+// [128 r, 128 r + 128) of the B block into its own shared memory (plain TMA, one
+// tile per CTA, nothing broadcast), and the leader CTA's MMA thread issues
+// M = 256, N = 256 MMAs that read A and B from both CTAs and accumulate each CTA's
+// 128 rows in that CTA's TMEM. Against one CTA with 128 x 256 tiles, each SM stages
+// half as much of B per output (32 KB stages instead of 48 KB, so six stages fit) and
+// the L2 serves half the B traffic.
+//   * both CTAs' copies of stage s complete on the LEADER's full[s] (the peer's TMA
+//     names the leader's barrier); the leader's producer expects both CTAs' bytes;
+//   * the MMA commits arrive on empty[s] and tfull[acc] in BOTH CTAs (commit with a
+//     two-CTA mask), so each producer and each epilogue waits on its own barriers;
+//   * every epilogue warp of both CTAs arrives on the leader's tempty[acc] once it
+//     has drained its columns (16 arrivals), which the MMA thread waits for;
+//   * TMEM is allocated and freed by warp 1 of both CTAs together, after a cluster
+//     barrier at the end, when no MMA reads the peer's shared memory any more.
+constexpr int kPairStages = 6;
+constexpr int kPairBM = 256, kPairBN = 256;
+constexpr int kPairBHalf = 128;                           // B columns per CTA
+constexpr int kPairABytes = 128 * BK * 2;                 // 16 KB
+constexpr int kPairBBytes = BK * kPairBHalf * 2;          // 16 KB (two 64 x 64 boxes)
+constexpr int kPairStageBytes = kPairABytes + kPairBBytes;
+constexpr int kPairEpiArrivals = 2 * kEpiWarps;           // one per epilogue warp, both CTAs
+constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 256 + kEpiBytes + 1024;
+static_assert(kPairSmemBytes <= 227 * 1024, "pair GEMM shared memory");
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tc_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+             T* __restrict__ C, int M, int N, int K, int64_t ldc, unsigned* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPairStages * kPairStageBytes);
+  uint64_t* empty = full + kPairStages;
+  uint64_t* tfull = empty + kPairStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint32_t* stage_out = reinterpret_cast<uint32_t*>(smem + kPairStages * kPairStageBytes + 256);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cta_rank_in_cluster();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
+  const int num_m = (M + kPairBM - 1) / kPairBM, num_n = (N + kPairBN - 1) / kPairBN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kPairEpiArrivals);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+    tc_fence_before();
+  }
+  // both CTAs' barriers are initialised (and TMEM allocated) before either CTA's
+  // copies or commits can reach the other
+  cluster_barrier();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs): this CTA's half of A and of B
+      // (after a pitch copy this grid starts early as its programmatic dependent: the
+      // set-up above overlaps the copy's tail, the first load waits for its result)
+      pdl_wait_primary();
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, err)) { ok = false; break; }
+          uint8_t* sa = smem + stage * kPairStageBytes;
+          const uint32_t bar = cluster_map(&full[stage], 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kPairStageBytes);
+          tma_load_2d_pair(sa, &tmA, kb * BK, mb * kPairBM + static_cast<int>(rank) * 128, bar);
+#pragma unroll
+          for (int j = 0; j < kPairBHalf / 64; ++j)
+            tma_load_2d_pair(sa + kPairABytes + j * kBBoxBytes, &tmB,
+                             nb * kPairBN + static_cast<int>(rank) * kPairBHalf + j * 64, kb * BK,
+                             bar);
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+      }
+      // every slot released once more = every copy issued has landed and been consumed
+      for (int s = 0; s < kPairStages && ok; ++s) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, err)) break;
+        if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader CTA only)
+      constexpr uint32_t idesc = idesc_f16(kPairBM, kPairBN, std::is_same<T, __nv_bfloat16>::value,
+                                           false, true);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs) {
+        if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * kPairBN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + stage * kPairStageBytes);
+          const uint32_t b0 = a0 + kPairABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = smem_desc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(b0 + k * 16 * 128, kBBoxBytes, 1024);
+            umma_f16_ss_pair(d, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+        umma_commit_pair(&tfull[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      umma_commit_pair(drain, 0x1);
+      mbar_wait(drain, 0, err);
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows of the pair's tile
+    const int quarter = warp % 4;
+    const int chunk0 = (warp - 2) / 4;
+    const int r_in_tile = static_cast<int>(rank) * 128 + quarter * 32 + lane;
+    const bool vec_ok = (ldc % 8 == 0) && (reinterpret_cast<uintptr_t>(C) % 16 == 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < tiles; t += npairs) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const bool ok = mbar_wait(&tfull[acc], acc_phase, err);
+      if (!__all_sync(kFull, ok)) break;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(mb) * kPairBM + r_in_tile;
+      T* crow = C + row * ldc;
+#pragma unroll 1
+      for (int c = chunk0; c < kPairBN / 32; c += 2) {
+        uint32_t r[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kPairBN + c * 32, r);
+        tmem_wait_ld();
+        const int col0 = nb * kPairBN + c * 32;
+        if (vec_ok) {
+          if (row < M && col0 < N) store_row32<T>(crow + col0, r, N - col0, true);
+        } else if (col0 < N) {
+          uint32_t* st = stage_out + (warp - 2) * (32 * 17);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            st[lane * 17 + i] = pack2_t<T>(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+          __syncwarp();
+          const int64_t row0 = static_cast<int64_t>(mb) * kPairBM + rank * 128 + quarter * 32;
+          const bool col_ok = col0 + lane < N;
+#pragma unroll 4
+          for (int rr = 0; rr < 32; ++rr) {
+            const uint32_t w = st[rr * 17 + lane / 2];
+            const uint16_t h = static_cast<uint16_t>((lane & 1) ? (w >> 16) : (w & 0xFFFF));
+            if (col_ok && row0 + rr < M)
+              *reinterpret_cast<uint16_t*>(C + (row0 + rr) * ldc + col0 + lane) = h;
+          }
+          __syncwarp();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(cluster_map(&tempty[acc], 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+  __syncthreads();
+  // no CTA leaves (or frees TMEM) while the pair's MMAs may still touch its memory
+  cluster_barrier();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
+  }
+}
+
 // dst (rows x cols_pad) = src (rows x cols) with zero columns appended; cols_pad is a
 // multiple of 8, so every thread writes one aligned 16-byte vector of a dst row
 // (coalesced 2-byte reads of the unaligned source row).
@@ -255,6 +457,8 @@ __device__ __forceinline__ uint32_t word_at(const uint4& a, const uint4& b, int 
 template <typename T>
 __global__ void pad_cols(const T* __restrict__ src, T* __restrict__ dst, int64_t rows,
                          int64_t cols, int64_t cols_pad) {
+  // the GEMM that reads dst may launch now; its loads wait for this grid to finish
+  pdl_launch_dependents();
   const int64_t nvec = cols_pad / 8;
   const uintptr_t src_lo = reinterpret_cast<uintptr_t>(src);
   const uintptr_t src_hi = src_lo + static_cast<uintptr_t>(rows * cols) * 2;
@@ -315,6 +519,15 @@ Staging staging(const void* A, const void* B, int64_t M, int64_t N, int64_t K) {
   return s;
 }
 
+// KPB_GEMM_PAIR=0 in the environment selects the one-CTA kernel for every shape.
+bool pair_disabled() {
+  static const bool off = [] {
+    const char* v = std::getenv("KPB_GEMM_PAIR");
+    return v != nullptr && v[0] == '0';
+  }();
+  return off;
+}
+
 template <typename T>
 int launch_tc(const T* A, const T* B, T* C, int64_t M, int64_t N, int64_t K, void* ws,
               size_t ws_bytes, unsigned* err, cudaStream_t s) {
@@ -344,17 +557,54 @@ int launch_tc(const T* A, const T* B, T* C, int64_t M, int64_t N, int64_t K, voi
     b = bp;
     ldb = st.np;
   }
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tb_pair;
   if (int rc = make_tmap_2d_sw128(&ta, a, bf16, static_cast<uint64_t>(lda), M, lda * 2, BM)) return rc;
   if (int rc = make_tmap_2d_sw128(&tb, b, bf16, static_cast<uint64_t>(ldb), K, ldb * 2, BK)) return rc;
+  tb_pair = tb;  // the same 64 x 64 boxes of B
+  // with a padded A the K loop runs over the zero-padded width (B reads zeros there)
+  if (M > BM && !pair_disabled()) {
+    auto kern = gemm_tc_pair<T>;
+    KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  kPairSmemBytes));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (st.pad_a || st.pad_b) ? 2 : 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kPairSmemBytes;
+    cfg.stream = s;
+    cfg.gridDim = dim3(static_cast<unsigned>(sms / 2 * 2));
+    int active = 0;
+    KPB_CUDA(cudaOccupancyMaxActiveClusters(&active, kern, &cfg));
+    if (active < 1) return fail(KPB_ECUDA, "matmul: the CTA-pair kernel does not fit");
+    const int64_t pair_tiles = cdiv(M, kPairBM) * cdiv(N, kPairBN);
+    const int64_t pairs = std::min<int64_t>(pair_tiles, active);
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    KPB_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb_pair, C, static_cast<int>(M),
+                                static_cast<int>(N), static_cast<int>(lda), N, err));
+    return KPB_OK;
+  }
   auto kern = gemm_tc<T>;
   KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
   const int64_t tiles = cdiv(M, BM) * cdiv(N, BN);
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
-  // with a padded A the K loop runs over the zero-padded width (B reads zeros there)
-  kern<<<grid, kThreads, kSmemBytes, s>>>(ta, tb, C, static_cast<int>(M), static_cast<int>(N),
-                                         static_cast<int>(lda), N, err);
-  KPB_LAUNCHED("matmul tcgen05");
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (st.pad_a || st.pad_b) ? 1 : 0;
+  cfg.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(tiles, sms)));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = s;
+  KPB_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, C, static_cast<int>(M), static_cast<int>(N),
+                              static_cast<int>(lda), N, err));
   return KPB_OK;
 }
 

@@ -14,8 +14,13 @@
 //              read and one write per element. The arithmetic is packed (3-input max,
 //              f32x2 FMA/add/mul) and exp2 runs on the MUFU directly, about 4.5
 //              instructions per element, so the kernel stays memory-bound.
-//              Rows longer than 1024 threads x 24 (fp32) / 32 (16-bit) values take
-//              "two-pass": online (max, sum) in one read, normalise in a second.
+//              Rows longer than 1024 threads x 24 (fp32) / 32 (16-bit) values are
+//              split over a thread-block cluster of 2, 4 or 8 CTAs ("cluster"): each
+//              CTA runs the same ring on its slice of the row and the row's max and
+//              sum are merged through distributed shared memory, so such rows still
+//              cost one HBM read and one write. Rows beyond 8 CTAs' registers
+//              (196,608 fp32 / 262,144 16-bit values) take "two-pass": online
+//              (max, sum) in one read, normalise in a second.
 //
 // Rows need not start on a 16-byte boundary (fp32 N=4097 rows are 16388 bytes):
 // each row is viewed through the aligned window that contains it. Whole 16-byte
@@ -129,6 +134,55 @@ __device__ __forceinline__ void vscale(float (&f)[VN], float inv) {
   }
 }
 
+// ---- row statistics with one block barrier
+//
+// Each warp takes the max of its values, exponentiates them against it (in log2
+// units: f <- 2^(x*log2e - ml_w)) and sums them; lane 0 posts (ml_w, d_w) for its
+// warp, with d_w = -1 when the warp's copy wait gave up. After ONE barrier every warp
+// merges the posted pairs the same way (lane i takes warp i's pair; a shuffle max and
+// a shuffle sum of d_i * 2^(ml_i - ML)), so all warps get the same (ML, D) bits, and a
+// value's softmax is f * 2^(ml_w - ML) / D. The posts alternate between two buffers
+// by row parity: a warp writes row r+2's post only after the barrier of row r+1,
+// which every warp reaches after reading row r's posts.
+struct RowStats {
+  float ml_warp;  // this warp's max (log2 units)
+  float ml;       // the block's max (log2 units)
+  float d;        // the block's sum of 2^(x*log2e - ml)
+  bool ok;        // no warp's copy wait gave up
+};
+
+template <int V, int VN>
+__device__ __forceinline__ RowStats block_row_stats(float (&f)[V][VN], bool ok, float2* post) {
+  const int lane = threadIdx.x & (kWarp - 1), wid = threadIdx.x / kWarp;
+  const int nwarps = blockDim.x / kWarp;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < V; ++k) mx = vmax<VN>(f[k], mx);
+  mx = warp_max(mx);
+  RowStats r;
+  r.ml_warp = mx * kLog2e;
+  const float neg = r.ml_warp == -INFINITY ? 0.f : -r.ml_warp;
+  float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < V; ++k) acc = vexp<VN>(f[k], acc, neg);
+  const float d = warp_sum(acc.x + acc.y);
+  const bool wok = __all_sync(kFull, ok);
+  if (lane == 0) post[wid] = make_float2(r.ml_warp, wok ? d : -1.f);
+  __syncthreads();
+  const float2 pw = lane < nwarps ? post[lane] : make_float2(-INFINITY, 0.f);
+  r.ok = !__any_sync(kFull, pw.y < 0.f);
+  r.ml = warp_max(pw.x);
+  const float term = pw.x == -INFINITY ? 0.f : pw.y * ex2f(pw.x - r.ml);
+  r.d = warp_sum(term);
+  return r;
+}
+
+// factor that turns this warp's 2^(x*log2e - ml_warp) into softmax values, given the
+// row's max ml and sum d (both in the same units)
+__device__ __forceinline__ float warp_scale(float ml_warp, float ml, float d) {
+  return ml_warp == -INFINITY ? 0.f : ex2f(ml_warp - ml) / d;
+}
+
 template <typename T, int V, bool kAligned>
 __global__ void __launch_bounds__(1024)
 softmax_staged(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N, int stages,
@@ -137,7 +191,7 @@ softmax_staged(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N, int
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint8_t* ring = smem + 128;
-  __shared__ float s_max[kWarp], s_sum[kWarp];
+  __shared__ float2 post[2][kWarp];
 
   const uintptr_t xbase = reinterpret_cast<uintptr_t>(x);
   const uintptr_t xend = xbase + static_cast<uintptr_t>(M) * N * sizeof(T);
@@ -189,7 +243,6 @@ softmax_staged(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N, int
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x, ++it) {
     const int slot = it % stages;
     const bool ok = mbar_wait(&full[slot], static_cast<uint32_t>((it / stages) & 1), err);
-    if (__syncthreads_or(!ok)) return;
 
     const RowView rv = row_view<T>(xbase + static_cast<uintptr_t>(row) * row_bytes, N);
     int vlo = 0, vhi = rv.nv;
@@ -198,7 +251,6 @@ softmax_staged(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N, int
     const T* xr = x + row * N;
 
     float f[V][VN];
-    float mx = -INFINITY;
 #pragma unroll
     for (int k = 0; k < V; ++k) {
       const int j = threadIdx.x + k * blockDim.x;
@@ -221,21 +273,15 @@ softmax_staged(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N, int
           }
         }
       }
-      mx = vmax<VN>(f[k], mx);
     }
-    mx = block_reduce<true>(mx, s_max);
+    const RowStats st = block_row_stats<V, VN>(f, ok, post[it & 1]);
+    if (!st.ok) return;  // the same decision in every warp
     // every thread has read its slice of the slot: refill it with a later row
     if (threadIdx.x == 0) {
       const int64_t nr = row + static_cast<int64_t>(stages) * gridDim.x;
       if (nr < M) issue(nr, slot);
     }
-
-    const float neg_ml = -(mx * kLog2e);
-    float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int k = 0; k < V; ++k) acc = vexp<VN>(f[k], acc, neg_ml);
-    const float sum = block_reduce<false>(acc.x + acc.y, s_sum);
-    const float inv = 1.f / sum;
+    const float scale = warp_scale(st.ml_warp, st.ml, st.d);
 
     T* yr = y + row * N;
     uint8_t* ywin = reinterpret_cast<uint8_t*>(reinterpret_cast<uintptr_t>(yr) - rv.a * sizeof(T));
@@ -243,10 +289,208 @@ softmax_staged(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N, int
     for (int k = 0; k < V; ++k) {
       const int j = threadIdx.x + k * blockDim.x;
       if (j >= rv.nv) continue;
-      vscale<VN>(f[k], inv);
+      vscale<VN>(f[k], scale);
       const int e0 = j * VN - rv.a;
       if (kAligned || (y_vec && e0 >= 0 && e0 + VN <= N)) {
         st_stream(ywin + j * 16, pack<T>(f[k]));
+      } else {
+#pragma unroll
+        for (int l = 0; l < VN; ++l)
+          if (e0 + l >= 0 && e0 + l < N) yr[e0 + l] = from_f<T>(f[k][l]);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ variant 2: cluster
+
+constexpr int kMaxCluster = 8;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t n;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(n));
+  return n;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t c;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(c));
+  return c;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+  uint32_t c;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(c));
+  return c;
+}
+// Every thread of every CTA of the cluster (used once, before the first remote store:
+// every CTA is running and its barriers are initialised).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Store v into CTA `peer`'s copy of *slot and count its 8 bytes on that CTA's copy of
+// *bar (slot and bar sit at the same offsets in every CTA of the cluster).
+__device__ __forceinline__ void dsmem_send(const float2* slot, const uint64_t* bar, uint32_t peer,
+                                           float2 v) {
+  uint32_t raddr, rbar;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(raddr) : "r"(smem_u32(slot)), "r"(peer));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(smem_u32(bar)), "r"(peer));
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
+               :: "r"(raddr), "f"(v.x), "f"(v.y), "r"(rbar) : "memory");
+}
+
+// Row r of the matrix is processed by cluster (r mod clusters): CTA c of the cluster
+// owns vectors [c*nvc, (c+1)*nvc) of the row's aligned window. Each CTA keeps its own
+// ring of slice buffers, exactly as softmax_staged does for whole rows, and computes
+// its slice's (max, sum) with one block barrier (block_row_stats). Thread 0 then sends
+// that pair to every CTA of the cluster (st.async into slot [rank] of each CTA's
+// array, completing 8 bytes on that CTA's mbarrier); each CTA waits (bounded) until
+// all C pairs have landed and merges them in rank order, so every CTA normalises with
+// the same bits: one exchange per row, and no cluster-wide barrier, so the row's
+// streaming global stores never have to drain before it. Slots and mbarriers
+// alternate between two sets by row parity: a CTA sends row r+2's pair only after it
+// has received every CTA's pair of row r+1, which each CTA sends only after it has
+// read its row-r slots. A CTA whose copy wait gave up sends a failure flag (a
+// negative sum), and every CTA then leaves the loop at the same row; a CTA whose
+// exchange wait gives up leaves too (its peers' waits then give up in turn).
+template <typename T, int V, bool kAligned>
+__global__ void __launch_bounds__(1024)
+softmax_cluster(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N, int nvc,
+                int stages, uint32_t stage_bytes, unsigned* err) {
+  constexpr int VN = Vec<T>::kN;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint8_t* ring = smem + 128;
+  __shared__ float2 post[2][kWarp];
+  __shared__ __align__(8) float2 c_stat[2][kMaxCluster];
+  __shared__ __align__(8) uint64_t xbar[2];
+
+  const int C = static_cast<int>(cluster_size());
+  const int crank = static_cast<int>(cluster_rank());
+  const int64_t first = cluster_id(), step = cluster_count();
+  const uintptr_t xbase = reinterpret_cast<uintptr_t>(x);
+  const uintptr_t xend = xbase + static_cast<uintptr_t>(M) * N * sizeof(T);
+  const uintptr_t ok_lo = (xbase + 15) & ~uintptr_t(15);
+  const uintptr_t ok_hi = xend & ~uintptr_t(15);
+  const size_t row_bytes = static_cast<size_t>(N) * sizeof(T);
+  const bool y_vec = ((reinterpret_cast<uintptr_t>(y) ^ xbase) & 15) == 0;
+  const uint32_t xchg_bytes = static_cast<uint32_t>(C) * sizeof(float2);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+    for (int b = 0; b < 2; ++b) mbar_init(&xbar[b], 1);
+    fence_mbar_init();
+  }
+  // every CTA of the cluster is running, with its barriers initialised, before any
+  // CTA stores into another's shared memory
+  cluster_sync_all();
+  const uint64_t policy = l2_evict_first_policy();
+
+  // this CTA's slice of a row window, clipped to the bytes a bulk copy may touch
+  auto slice = [&](const RowView& rv, int& s0, int& s1, int& vlo, int& vhi) {
+    s0 = crank * nvc;
+    s1 = min(rv.nv, s0 + nvc);
+    const uintptr_t cs0 = rv.win + static_cast<uintptr_t>(s0) * 16;
+    const uintptr_t ce0 = rv.win + static_cast<uintptr_t>(s1) * 16;
+    const uintptr_t cs = cs0 > ok_lo ? cs0 : ok_lo;
+    const uintptr_t ce = ce0 < ok_hi ? ce0 : ok_hi;
+    vlo = static_cast<int>((cs - rv.win) / 16);
+    vhi = ce > cs ? static_cast<int>((ce - rv.win) / 16) : vlo;
+  };
+  auto issue = [&](int64_t row, int slot) {
+    const RowView rv = row_view<T>(xbase + static_cast<uintptr_t>(row) * row_bytes, N);
+    int s0, s1, vlo, vhi;
+    slice(rv, s0, s1, vlo, vhi);
+    if (vhi > vlo) {
+      const uint32_t bytes = static_cast<uint32_t>(vhi - vlo) * 16;
+      mbar_arrive_expect_tx(&full[slot], bytes);
+      bulk_g2s(ring + size_t(slot) * stage_bytes + (vlo - s0) * 16,
+               reinterpret_cast<const void*>(rv.win + static_cast<uintptr_t>(vlo) * 16), bytes,
+               &full[slot], policy);
+    } else {
+      mbar_arrive(&full[slot]);
+    }
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      const int64_t r = first + static_cast<int64_t>(s) * step;
+      if (r < M) issue(r, s);
+    }
+  }
+
+  int it = 0;
+  for (int64_t row = first; row < M; row += step, ++it) {
+    const int slot = it % stages;
+    const int par = it & 1;
+    const uint32_t xphase = static_cast<uint32_t>((it >> 1) & 1);
+    const bool ok = mbar_wait(&full[slot], static_cast<uint32_t>((it / stages) & 1), err);
+
+    const RowView rv = row_view<T>(xbase + static_cast<uintptr_t>(row) * row_bytes, N);
+    int s0, s1, vlo, vhi;
+    slice(rv, s0, s1, vlo, vhi);
+    if (kAligned) {
+      vlo = s0;
+      vhi = s1;
+    }
+    const uint8_t* stage = ring + size_t(slot) * stage_bytes;
+    const T* xr = x + row * N;
+
+    float f[V][VN];
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int j = s0 + static_cast<int>(threadIdx.x) + k * static_cast<int>(blockDim.x);
+      const int e0 = j * VN - rv.a;
+      if (j < s1 && j >= vlo && j < vhi && (kAligned || (e0 >= 0 && e0 + VN <= N))) {
+        unpack<T>(*reinterpret_cast<const uint4*>(stage + (j - s0) * 16), f[k]);
+      } else {
+#pragma unroll
+        for (int l = 0; l < VN; ++l) {
+          const int e = e0 + l;
+          f[k][l] = (j < s1 && e >= 0 && e < N) ? to_f(xr[e]) : -INFINITY;
+        }
+      }
+    }
+    // this CTA's (max, sum) of its slice, after one block barrier
+    const RowStats st = block_row_stats<V, VN>(f, ok, post[par]);
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(&xbar[par], xchg_bytes);
+      for (int p = 0; p < C; ++p)
+        dsmem_send(&c_stat[par][crank], &xbar[par], p, make_float2(st.ml, st.ok ? st.d : -1.f));
+      const int64_t nr = row + static_cast<int64_t>(stages) * step;
+      if (st.ok && nr < M) issue(nr, slot);
+    }
+    if (!mbar_wait(&xbar[par], xphase, err)) break;
+    // merge the cluster's pairs in rank order: the same bits in every CTA
+    float gml = -INFINITY;
+    bool failed = false;
+    for (int p = 0; p < C; ++p) {
+      const float2 v = c_stat[par][p];
+      gml = fmaxf(gml, v.x);
+      failed |= v.y < 0.f;
+    }
+    if (failed) break;  // the same decision in every CTA of the cluster
+    float gd = 0.f;
+    for (int p = 0; p < C; ++p) {
+      const float2 v = c_stat[par][p];
+      if (v.x != -INFINITY) gd += v.y * ex2f(v.x - gml);
+    }
+    const float scale = warp_scale(st.ml_warp, gml, gd);
+
+    T* yr = y + row * N;
+    uint8_t* ywin = reinterpret_cast<uint8_t*>(reinterpret_cast<uintptr_t>(yr) - rv.a * sizeof(T));
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int j = s0 + static_cast<int>(threadIdx.x) + k * static_cast<int>(blockDim.x);
+      if (j >= s1) continue;
+      vscale<VN>(f[k], scale);
+      const int e0 = j * VN - rv.a;
+      if (kAligned || (y_vec && e0 >= 0 && e0 + VN <= N)) {
+        st_stream(ywin + static_cast<size_t>(j) * 16, pack<T>(f[k]));
       } else {
 #pragma unroll
         for (int l = 0; l < VN; ++l)
@@ -362,8 +606,10 @@ int64_t window_vectors(bool aligned, int64_t N) {
   return aligned ? cdiv(N, VN) : (N + 2 * VN - 2) / VN;
 }
 
+// `max_ctas_per_sm` caps the CTAs the ring is sized for (the cluster kernel runs at
+// 64 registers per thread, so at most 1024 threads per SM).
 template <typename T>
-StagedPlan plan_staged(int64_t nv_max) {
+StagedPlan plan_staged(int64_t nv_max, int max_ctas_per_sm = 32) {
   StagedPlan p{};
   // Cost of one row per CTA ~ threads * (V + 5): V vectors of element work plus a
   // fixed per-row share (two block reductions, the slot wait, the refill) worth about
@@ -386,7 +632,7 @@ StagedPlan plan_staged(int64_t nv_max) {
   const int64_t smem_per_sm = 220 * 1024;
   p.stages = 1;
   p.ctas_per_sm = 1;
-  for (int c = 2048 / p.threads; c >= 1; --c) {
+  for (int c = std::min(2048 / p.threads, max_ctas_per_sm); c >= 1; --c) {
     const int64_t st = std::min<int64_t>(kMaxStages, smem_per_sm / c / (p.stage_bytes + 1024));
     if (st >= 2 || (c == 1 && st >= 1)) {
       p.stages = static_cast<int>(st);
@@ -428,6 +674,50 @@ int dispatch_v(const T* x, T* y, int64_t M, int64_t N, const StagedPlan& p, unsi
   }
 }
 
+template <typename T, int V, bool kAligned>
+int launch_cluster(const T* x, T* y, int64_t M, int64_t N, int C, int nvc, const StagedPlan& p,
+                   unsigned* err, cudaStream_t s) {
+  auto kern = softmax_cluster<T, V, kAligned>;
+  const size_t smem = 128 + size_t(p.stages) * p.stage_bytes;
+  KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(smem)));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(C);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(p.threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  // as many clusters as can be resident at once (at most one per row)
+  cfg.gridDim = dim3(static_cast<unsigned>(C * sm_count()));
+  int active = 0;
+  KPB_CUDA(cudaOccupancyMaxActiveClusters(&active, kern, &cfg));
+  if (active < 1) return fail(KPB_ECUDA, "softmax: cluster kernel does not fit");
+  const int64_t clusters = std::min<int64_t>(M, active);
+  cfg.gridDim = dim3(static_cast<unsigned>(clusters * C));
+  KPB_CUDA(cudaLaunchKernelEx(&cfg, kern, x, y, M, static_cast<int>(N), nvc, p.stages,
+                              p.stage_bytes, err));
+  return KPB_OK;
+}
+
+template <typename T, bool kAligned>
+int dispatch_cluster(const T* x, T* y, int64_t M, int64_t N, int C, int nvc, const StagedPlan& p,
+                     unsigned* err, cudaStream_t s) {
+  constexpr bool f32 = sizeof(T) == 4;
+  switch (p.v) {
+    case 1: return launch_cluster<T, 1, kAligned>(x, y, M, N, C, nvc, p, err, s);
+    case 2: return launch_cluster<T, 2, kAligned>(x, y, M, N, C, nvc, p, err, s);
+    case 3: return launch_cluster<T, 3, kAligned>(x, y, M, N, C, nvc, p, err, s);
+    case 4: return launch_cluster<T, 4, kAligned>(x, y, M, N, C, nvc, p, err, s);
+    case 5: return launch_cluster<T, f32 ? 5 : 4, kAligned>(x, y, M, N, C, nvc, p, err, s);
+    default: return launch_cluster<T, f32 ? 6 : 4, kAligned>(x, y, M, N, C, nvc, p, err, s);
+  }
+}
+
 template <typename T>
 int launch(int variant, const T* x, T* y, int64_t M, int64_t N, unsigned* err, cudaStream_t s) {
   if (M == 0 || N == 0) return KPB_OK;
@@ -445,7 +735,24 @@ int launch(int variant, const T* x, T* y, int64_t M, int64_t N, unsigned* err, c
   }
   const bool aligned = rows_aligned(x, y, N);
   const int64_t nv_max = window_vectors<T>(aligned, N);
-  if (nv_max > 1024 * staged_max_v<T>()) {
+  const int64_t cta_max = 1024 * staged_max_v<T>();  // vectors one CTA keeps in registers
+  if (nv_max > cta_max) {
+    // the smallest cluster whose CTAs need at most 512 threads, so two CTAs share an
+    // SM and one row's exchange hides behind the other's arithmetic; else the
+    // smallest that fits at all
+    int C = 2;
+    while (C < kMaxCluster && cdiv(nv_max, C) > cta_max / 2) C *= 2;
+    if (cdiv(nv_max, C) > cta_max / 2) {
+      C = 2;
+      while (C < kMaxCluster && cdiv(nv_max, C) > cta_max) C *= 2;
+    }
+    if (cdiv(nv_max, C) <= cta_max) {
+      const int nvc = static_cast<int>(cdiv(nv_max, C));
+      StagedPlan p = plan_staged<T>(nvc);
+      p = plan_staged<T>(nvc, std::max(1, 1024 / p.threads));
+      return aligned ? dispatch_cluster<T, true>(x, y, M, N, C, nvc, p, err, s)
+                     : dispatch_cluster<T, false>(x, y, M, N, C, nvc, p, err, s);
+    }
     softmax_two_pass<T><<<static_cast<unsigned>(M), 1024, 0, s>>>(x, y, static_cast<int>(N));
     KPB_LAUNCHED("softmax two-pass");
     return KPB_OK;

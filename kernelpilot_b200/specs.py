@@ -14,7 +14,8 @@ additions are all additive:
 * ``VECTOR_ADD`` and ``LAYERNORM`` (kernelpilot/specs.py:77-101, 214-250), the
   reference's remaining ``kp`` ops, with the same additions;
 * ``CONFIGS``: the headline workloads (the five of the reference's benchmark table,
-  plus causal attention, the elementwise add and LayerNorm) with their own generators
+  plus causal attention, a long-row softmax, the elementwise add and LayerNorm) with
+  their own generators
   (U(-1,1) for the reduction and the add, N(0,1)/sqrt(K) for the GEMM) next to
   ``make_inputs``.
 """
@@ -402,6 +403,9 @@ CONFIGS: dict[str, Workload] = {w.key: w for w in [
              _uniform_pm1, "hbm", "full sum fp32, n = 2^28+1, U(-1,1)"),
     Workload("softmax_bf16_65536x32768", "softmax", (65536, 32768), torch.bfloat16,
              _softmax_inputs, "hbm", "row softmax bf16 [65536, 32768], N(0,1)*30"),
+    Workload("softmax_bf16_4096x131072", "softmax", (4096, 131072), torch.bfloat16,
+             _softmax_inputs, "hbm",
+             "long-row softmax bf16 [4096, 131072] (a cluster of CTAs per row), N(0,1)*30"),
     Workload("gemm_bf16_8192", "matmul", (8192, 8192, 8192), torch.bfloat16,
              _matmul_scaled, "tensor", "GEMM bf16 8192^3, N(0,1)/sqrt(K)"),
     Workload("gemm_bf16_4097x4097x4096", "matmul", (4097, 4097, 4096), torch.bfloat16,

@@ -12,6 +12,7 @@ from kernelpilot_b200.specs import CONFIGS
     ("reduce_f32_2p28p1", 2),             # persistent level + one-CTA finish
     ("softmax_f32_4096x4097", 1),
     ("softmax_bf16_65536x32768", 1),
+    ("softmax_bf16_4096x131072", 1),
     ("gemm_bf16_8192", 1),
     ("gemm_bf16_4097x4097x4096", 2),      # B's 8194-byte rows take a pitch copy first
     ("attn_bf16_b8h32s4096d128", 1),

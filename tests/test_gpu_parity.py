@@ -87,10 +87,18 @@ def test_golden_vectors_every_variant(op):
 
 EDGE = [
     ("softmax", (33, 4097), torch.float32),      # rows start at 4-byte offsets
-    ("softmax", (7, 24577), torch.float32),      # just past the staged limit -> two-pass
-    ("softmax", (3, 100003), torch.float32),     # long misaligned rows, two-pass
+    ("softmax", (7, 24577), torch.float32),      # just past one CTA's registers -> cluster of 2
+    ("softmax", (3, 100003), torch.float32),     # long misaligned rows, cluster of 8
     ("softmax", (9, 32768), torch.bfloat16),     # staged, 4 vectors per thread
-    ("softmax", (5, 32769), torch.bfloat16),     # two-pass, misaligned
+    ("softmax", (5, 32769), torch.bfloat16),     # cluster of 2, misaligned
+    ("softmax", (64, 131072), torch.bfloat16),   # cluster of 4, aligned
+    ("softmax", (64, 65537), torch.float32),     # cluster of 4, rows at 4-byte offsets
+    ("softmax", (33, 100000), torch.float16),    # cluster of 4, 8 rows per cluster pass
+    ("softmax", (7, 196608), torch.float32),     # cluster of 8, exactly full
+    ("softmax", (3, 196609), torch.float32),     # one value past 8 CTAs -> two-pass
+    ("softmax", (5, 262144), torch.bfloat16),    # cluster of 8, 16-bit limit
+    ("softmax", (2, 262153), torch.bfloat16),    # past it, misaligned -> two-pass
+    ("softmax", (1000, 40000), torch.bfloat16),  # more rows than resident clusters
     ("softmax", (300, 4095), torch.float16),     # odd rows, many CTAs per SM
     ("softmax", (1500, 1), torch.float32),       # one element per row
     ("layernorm", (33, 4097), torch.float32),    # rows at 4-byte offsets -> block per row
