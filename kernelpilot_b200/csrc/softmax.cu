@@ -263,9 +263,17 @@ softmax_staged(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N, int
         }
       } else {
         const int e0 = j * VN - rv.a;
-        if (j >= vlo && j < vhi && e0 >= 0 && e0 + VN <= N) {
+        if (j >= vlo && j < vhi) {
+          // the window vector is in the stage; a vector straddling the row's start
+          // or end keeps only the row's elements
           unpack<T>(*reinterpret_cast<const uint4*>(stage + j * 16), f[k]);
+          if (e0 < 0 || e0 + VN > N) {
+#pragma unroll
+            for (int l = 0; l < VN; ++l)
+              if (e0 + l < 0 || e0 + l >= N) f[k][l] = -INFINITY;
+          }
         } else {
+          // outside the copied span (the first or last vector of the whole matrix)
 #pragma unroll
           for (int l = 0; l < VN; ++l) {
             const int e = e0 + l;
@@ -445,8 +453,13 @@ softmax_cluster(const T* __restrict__ x, T* __restrict__ y, int64_t M, int N, in
     for (int k = 0; k < V; ++k) {
       const int j = s0 + static_cast<int>(threadIdx.x) + k * static_cast<int>(blockDim.x);
       const int e0 = j * VN - rv.a;
-      if (j < s1 && j >= vlo && j < vhi && (kAligned || (e0 >= 0 && e0 + VN <= N))) {
+      if (j < s1 && j >= vlo && j < vhi) {
         unpack<T>(*reinterpret_cast<const uint4*>(stage + (j - s0) * 16), f[k]);
+        if (!kAligned && (e0 < 0 || e0 + VN > N)) {
+#pragma unroll
+          for (int l = 0; l < VN; ++l)
+            if (e0 + l < 0 || e0 + l >= N) f[k][l] = -INFINITY;
+        }
       } else {
 #pragma unroll
         for (int l = 0; l < VN; ++l) {
