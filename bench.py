@@ -25,7 +25,9 @@ roofline   rank 0's algorithmic bytes/FLOPs per call over its measured device ti
 check      the reduction's result against the float64 sum of the global vector (the
            ranks' float64 shard sums, all-reduced), with the spec's tolerance.
 configs    the other headline workloads, split the same way, device-timed; at N = 1
-           each row also carries its e2e number and the reference's CPU path.
+           each row also carries its e2e number, the reference's CPU path and the
+           reference's own Triton kernels for the op timed on the same inputs
+           ("triton_twins", a comparison, not this library).
 cpu_baseline  the reference's CPU path (the PyTorch built-in its spec names as
            ``baseline``) on this box's host cores, rank 0 at N=1 only.
 --impl reference  runs only that CPU path, on the same job, and prints its line.
@@ -292,7 +294,8 @@ def time_e2e(w: Workload, local: tuple, steps: int, world: int, exchange=None) -
 def spot_check(w: Workload, local: tuple, out: torch.Tensor) -> dict:
     """The reference gate (kernelpilot's ``compare`` with the spec's tolerance) on a
     slice of this rank's output: 64 rows (softmax, LayerNorm, GEMM), one (batch,
-    head) slice (attention), the first 2^20 elements (elementwise add)."""
+    head) slice (attention), the first 2^20 elements (elementwise add), or the whole
+    sum of this rank's shard (reduction)."""
     from kernelpilot_b200 import harness
 
     spec = w.spec
@@ -309,6 +312,8 @@ def spot_check(w: Workload, local: tuple, out: torch.Tensor) -> dict:
     elif w.kernel == "vector_add":
         n = min(1 << 20, local[0].numel())
         ins, got, shape = tuple(t[:n] for t in local), out[:n], (n,)
+    elif w.kernel == "reduce_sum":
+        ins, got, shape = tuple(local), out.reshape(()), (local[0].numel(),)
     else:
         return {}
     tol = spec.tolerance(shape, w.dtype)
@@ -400,10 +405,63 @@ def run_reference(args, rk: kdist.Rank) -> int:
     return 0
 
 
+# ------------------------------------------------------------------ Triton twins
+
+def time_calls(fn, inputs: tuple, calls: int) -> tuple[float, object]:
+    """Mean device ms per call of ``fn`` over ``calls`` back-to-back calls (inputs
+    larger than L2 or flushed by the caller's convention), and the last output."""
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = None
+    t0.record()
+    for _ in range(calls):
+        out = fn(*inputs)
+    t1.record()
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / calls, out
+
+
+def triton_twins(w: Workload, inputs: tuple, peak: float) -> dict:
+    """The reference's own Triton kernels for this op (kernelpilot/triton_kernels/*,
+    registered as ``triton:<name>`` by kernelpilot/registry.py:58-65), compiled by
+    Triton for this GPU and timed on the same inputs: a comparison row, not part of
+    this library. Each gets the same spot check as our kernels."""
+    from kernelpilot_b200 import harness
+
+    if w.kernel == "attention_causal":
+        return {"note": "the reference has no causal Triton kernel"}
+    try:
+        impls = harness.reference().registry.triton_impls(w.kernel)
+    except Exception as e:  # reported, never hidden
+        return {"error": f"{type(e).__name__}: {e}"[:200]}
+    rows = {}
+    scale = 1e3 if w.bound == "hbm" else 1.0
+    for name, fn in impls.items():
+        try:
+            t_first = time.perf_counter()
+            fn(*inputs)  # compiles (and autotunes) once
+            torch.cuda.synchronize()
+            first_s = time.perf_counter() - t_first
+            est, _ = time_calls(fn, inputs, 1)
+            calls = int(min(20, max(3, 5.0 / max(est, 1e-3))))
+            time_calls(fn, inputs, 2)
+            ms, out = time_calls(fn, inputs, calls)
+            val = rate(w, ms)
+            rows[name] = {"value": round(val, 4), "ms": round(ms, 5), "calls": calls,
+                          "frac_of_peak": round(val * scale / peak, 4),
+                          "first_call_s": round(first_s, 2),
+                          "check": rounded(spot_check(w, inputs, out), 8)}
+            del out
+        except Exception as e:  # a Triton kernel that fails on this shape is reported
+            rows[name] = {"error": f"{type(e).__name__}: {e}"[:200]}
+        torch.cuda.empty_cache()
+    return rows
+
+
 # ------------------------------------------------------------------ the configs table
 
 def measure_row(w: Workload, rk: kdist.Rank, with_host: bool, warmup: int = 3,
-                budget_ms: float = 5.0, min_steps: int = 10, max_steps: int = 50) -> dict:
+                budget_ms: float = 5.0, min_steps: int = 10, max_steps: int = 50,
+                with_triton: bool = False) -> dict:
     """One workload of the table, split over the ranks like the headline: the whole
     job's rate over the max-over-ranks mean call time, the median call time beside
     it. The call count fills about ``budget_ms`` of device time (within [min_steps,
@@ -445,6 +503,8 @@ def measure_row(w: Workload, rk: kdist.Rank, with_host: bool, warmup: int = 3,
     if rk.rank == 0:
         row["check"] = rounded(spot_check(w, inputs, out), 8)
     del out
+    if with_triton and world == 1:
+        row["triton_twins"] = triton_twins(w, inputs, peak)
     if with_host:
         e2e = time_e2e(w, inputs, steps=3, world=world, exchange=exchange)
         row["e2e"] = rounded({k: v for k, v in e2e.items()}, 5)
@@ -471,6 +531,8 @@ def main() -> int:
     ap.add_argument("--configs", default="",
                     help="comma-separated workload keys for the table (default: all)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
+    ap.add_argument("--no-triton", action="store_true",
+                    help="skip the reference's Triton kernels in the configs table")
     ap.add_argument("--subset", type=int, default=0,
                     help="run a smaller instance: this many rows (softmax), rows of A (matmul), "
                          "batches (attention) or elements (reduce_sum); for profiling")
@@ -548,6 +610,7 @@ def main() -> int:
             "kernel": "rank 0's call on its shard, mean device time per call"}
 
     e2e = time_e2e(w, inputs, args.e2e_steps, rk.world, exchange) if args.e2e_steps > 0 else None
+    twins = triton_twins(w, inputs, peak) if (rk.world == 1 and not args.no_triton) else None
 
     configs = {}
     configs_clocks = None
@@ -563,7 +626,8 @@ def main() -> int:
                 if key == w.key:
                     continue
                 try:
-                    configs[key] = measure_row(CONFIGS[key], rk, with_host)
+                    configs[key] = measure_row(CONFIGS[key], rk, with_host,
+                                               with_triton=not args.no_triton)
                 except Exception as e:  # reported in the line, never hidden
                     configs[key] = {"error": f"{type(e).__name__}: {e}"[:300]}
                     if rk.world > 1:
@@ -603,6 +667,8 @@ def main() -> int:
     }
     if check:
         line["check"] = check
+    if twins:
+        line["triton_twins"] = twins
     if cpu:
         line["cpu_baseline"] = rounded(cpu)
     if configs:

@@ -6,7 +6,9 @@
 // Replaces the SIMT stages of kernelpilot's csrc/kernels/matmul.hip (:16-208):
 //   0 naive       one thread per C element
 //   1 smem_tiled  32x32 shared-memory tiles, one element per thread
-//   2 reg_tiled   64x64 CTA tile, BK=16, 4x4 outputs per thread
+//   2 reg_tiled   128x128 CTA tile, 8 k per step, 8x8 outputs per thread read from
+//                 shared memory as 16-byte vectors, the next step's tile prefetched
+//                 into registers while the current one is multiplied
 #include "kp_common.cuh"
 
 namespace kpb {
@@ -45,57 +47,90 @@ __global__ void __launch_bounds__(kT1 * kT1) mm_smem(const T* __restrict__ A,
   if (r < M && c < N) C[r * N + c] = from_f<T>(acc);
 }
 
-constexpr int kBM2 = 64, kBN2 = 64, kBK2 = 16;
+// ---- variant 2: 128 x 128 tiles, 8 x 8 outputs per thread
+//
+// 256 threads as a 16 x 16 grid. Thread (ty, tx) owns the rows {4ty..4ty+3} and
+// {64+4ty..64+4ty+3} and the same two column groups in tx: four 4x4 blocks, 64
+// accumulators. Shared memory holds the A tile transposed (k-major, [8][128]) and
+// the B tile as is ([8][128]), both as fp32, so each k step reads two float4 of A
+// and two float4 of B per thread: the 16 threads of a half-warp that share ty read
+// the same A vectors (a broadcast) and 16 consecutive B vectors. Two shared-memory
+// buffers alternate; the global loads of step s+1 are issued into registers before
+// step s is multiplied, so one barrier per step suffices.
+constexpr int kRT = 128, kRK = 8;
 
-// 256 threads as a 16x16 grid; thread (ty, tx) owns rows ty + 16*i and columns
-// tx + 16*j (i, j < 4), so both shared-memory reads are conflict-free broadcasts.
+template <typename T>
+struct TileLoader {
+  // A tile: 128 rows x 8 k; thread t takes row t / 2 and k (t % 2) * 4 .. + 3.
+  // B tile: 8 k x 128 columns; thread t takes k t / 32 and columns (t % 32) * 4 .. + 3.
+  float a[4], b[4];
+
+  __device__ __forceinline__ void load(const T* __restrict__ A, const T* __restrict__ B,
+                                       int64_t M, int64_t N, int64_t K, int64_t m0, int64_t n0,
+                                       int64_t k0, int tid) {
+    const int64_t ar = m0 + tid / 2, ak = k0 + (tid % 2) * 4;
+    const int64_t bk = k0 + tid / 32, bc = n0 + (tid % 32) * 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      a[i] = (ar < M && ak + i < K) ? to_f(A[ar * K + ak + i]) : 0.f;
+      b[i] = (bk < K && bc + i < N) ? to_f(B[bk * N + bc + i]) : 0.f;
+    }
+  }
+
+  __device__ __forceinline__ void store(float (*sa)[kRT], float (*sb)[kRT], int tid) const {
+    const int ar = tid / 2, ak = (tid % 2) * 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sa[ak + i][ar] = a[i];
+    *reinterpret_cast<float4*>(&sb[tid / 32][(tid % 32) * 4]) = make_float4(b[0], b[1], b[2], b[3]);
+  }
+};
+
 template <typename T>
 __global__ void __launch_bounds__(256) mm_regtile(const T* __restrict__ A,
                                                   const T* __restrict__ B, T* __restrict__ C,
                                                   int64_t M, int64_t N, int64_t K) {
-  __shared__ float sa[kBK2][kBM2 + 4];  // A tile stored k-major
-  __shared__ float sb[kBK2][kBN2 + 4];
+  __shared__ __align__(16) float sa[2][kRK][kRT];
+  __shared__ __align__(16) float sb[2][kRK][kRT];
   const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
-  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kBM2;
-  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kBN2;
-  float acc[4][4] = {};
-  for (int64_t k0 = 0; k0 < K; k0 += kBK2) {
-    // A tile: 64 rows x 16 k = 1024 elements, 4 per thread
+  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kRT;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kRT;
+  float acc[8][8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = tid + i * 256, rr = e / kBK2, kk = e % kBK2;
-      const int64_t gr = m0 + rr, gk = k0 + kk;
-      sa[kk][rr] = (gr < M && gk < K) ? to_f(A[gr * K + gk]) : 0.f;
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+  TileLoader<T> ld;
+  ld.load(A, B, M, N, K, m0, n0, 0, tid);
+  ld.store(sa[0], sb[0], tid);
+  __syncthreads();
+  const int64_t steps = (K + kRK - 1) / kRK;
+  for (int64_t st = 0; st < steps; ++st) {
+    const int cur = static_cast<int>(st & 1);
+    if (st + 1 < steps) ld.load(A, B, M, N, K, m0, n0, (st + 1) * kRK, tid);
+#pragma unroll
+    for (int k = 0; k < kRK; ++k) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&sa[cur][k][4 * ty]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&sa[cur][k][64 + 4 * ty]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&sb[cur][k][4 * tx]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&sb[cur][k][64 + 4 * tx]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
-    // B tile: 16 k x 64 cols
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = tid + i * 256, kk = e / kBN2, cc = e % kBN2;
-      const int64_t gk = k0 + kk, gc = n0 + cc;
-      sb[kk][cc] = (gk < K && gc < N) ? to_f(B[gk * N + gc]) : 0.f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < kBK2; ++kk) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = sa[kk][ty + 16 * i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = sb[kk][tx + 16 * j];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
-    }
+    if (st + 1 < steps) ld.store(sa[cur ^ 1], sb[cur ^ 1], tid);
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t r = m0 + ty + 16 * i;
+  for (int i = 0; i < 8; ++i) {
+    const int64_t r = m0 + (i < 4 ? 4 * ty + i : 64 + 4 * ty + i - 4);
     if (r >= M) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int64_t c = n0 + tx + 16 * j;
+    for (int j = 0; j < 8; ++j) {
+      const int64_t c = n0 + (j < 4 ? 4 * tx + j : 64 + 4 * tx + j - 4);
       if (c < N) C[r * N + c] = from_f<T>(acc[i][j]);
     }
   }
@@ -113,7 +148,7 @@ int matmul_simt_t(int variant, const T* A, const T* B, T* C, int64_t M, int64_t 
     if (grid.y > 65535) return fail(KPB_EUNSUPPORTED, "matmul variant 1: M too large");
     mm_smem<T><<<grid, block, 0, s>>>(A, B, C, M, N, K);
   } else {
-    const dim3 grid(static_cast<unsigned>(cdiv(N, kBN2)), static_cast<unsigned>(cdiv(M, kBM2)));
+    const dim3 grid(static_cast<unsigned>(cdiv(N, kRT)), static_cast<unsigned>(cdiv(M, kRT)));
     if (grid.y > 65535) return fail(KPB_EUNSUPPORTED, "matmul SIMT: M too large");
     mm_regtile<T><<<grid, 256, 0, s>>>(A, B, C, M, N, K);
   }

@@ -19,8 +19,6 @@
 // Shapes TMA cannot describe (a row pitch that is not a multiple of 16 bytes, e.g.
 // N = 4097, or an unaligned base) are first copied into a zero-padded, aligned
 // workspace; C is written with masked stores, so any M, N, K works.
-#include <cstdlib>
-
 #include "kp_common.cuh"
 #include "kp_sm100.cuh"
 
@@ -519,15 +517,6 @@ Staging staging(const void* A, const void* B, int64_t M, int64_t N, int64_t K) {
   return s;
 }
 
-// KPB_GEMM_PAIR=0 in the environment selects the one-CTA kernel for every shape.
-bool pair_disabled() {
-  static const bool off = [] {
-    const char* v = std::getenv("KPB_GEMM_PAIR");
-    return v != nullptr && v[0] == '0';
-  }();
-  return off;
-}
-
 template <typename T>
 int launch_tc(const T* A, const T* B, T* C, int64_t M, int64_t N, int64_t K, void* ws,
               size_t ws_bytes, unsigned* err, cudaStream_t s) {
@@ -562,7 +551,7 @@ int launch_tc(const T* A, const T* B, T* C, int64_t M, int64_t N, int64_t K, voi
   if (int rc = make_tmap_2d_sw128(&tb, b, bf16, static_cast<uint64_t>(ldb), K, ldb * 2, BK)) return rc;
   tb_pair = tb;  // the same 64 x 64 boxes of B
   // with a padded A the K loop runs over the zero-padded width (B reads zeros there)
-  if (M > BM && !pair_disabled()) {
+  if (M > BM) {
     auto kern = gemm_tc_pair<T>;
     KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   kPairSmemBytes));
