@@ -230,8 +230,17 @@ def make_step(w: Workload, inputs: tuple, exchange=None):
     return lambda: fn(*inputs)
 
 
-def time_steps(step, steps: int, flush: bool, world: int) -> tuple[float, list[float]]:
-    """(max-over-ranks total ms of the K steps, per-step ms on this rank)."""
+def time_steps(step, steps: int, flush: bool, world: int, align: bool = False
+               ) -> tuple[float, list[float]]:
+    """(max-over-ranks total ms of the K steps, per-step ms on this rank).
+
+    ``align`` is for steps that synchronise the ranks on the GPU (the reduction's
+    in-kernel exchange): the ranks' streams reach the first step at host-dependent
+    times, and every rank's exchange waits for the last one, so the first timed step
+    would carry that launch skew (up to ~0.25 ms at N = 4). The stream first idles
+    ~0.1 ms on the GPU, so the host can queue everything behind it, then runs one
+    untimed step that brings the ranks together on the device; the timed steps
+    follow it back to back."""
     from kernelpilot_b200.harness import flush_l2
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -239,6 +248,9 @@ def time_steps(step, steps: int, flush: bool, world: int) -> tuple[float, list[f
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
+    if align and world > 1:
+        torch.cuda._sleep(200_000)
+        step()
     for i in range(steps):
         if flush:
             flush_l2(clean=True)
@@ -487,7 +499,7 @@ def measure_row(w: Workload, rk: kdist.Rank, with_host: bool, warmup: int = 3,
         torch.distributed.all_reduce(est, op=torch.distributed.ReduceOp.MAX)
     steps = int(min(max_steps, max(min_steps, budget_ms / float(est.item()))))
     flush = sum(t.numel() * t.element_size() for t in inputs) < 2 * L2_BYTES
-    total, per = time_steps(step, steps, flush, world)
+    total, per = time_steps(step, steps, flush, world, align=isinstance(exchange, kdist.PeerSum))
     ms = total / steps
     peak, src = roofline_peak(w)
     val = rate(w, ms)
@@ -568,7 +580,8 @@ def main() -> int:
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
-        total_ms, per = time_steps(step, args.steps, flush, rk.world)
+        total_ms, per = time_steps(step, args.steps, flush, rk.world,
+                                   align=isinstance(exchange, kdist.PeerSum))
     ms = total_ms / args.steps
 
     check = None
