@@ -404,6 +404,13 @@ def run_reference(args, rk: kdist.Rank) -> int:
     if rk.rank != 0:
         return 0
     w = CONFIGS[args.workload]
+    from kernelpilot_b200 import harness
+
+    if not harness.available():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          f"the kernelpilot package is not installed under {harness.reference_root()}"}),
+              flush=True)
+        return 0
     cb = time_cpu(w, reps=args.steps + args.warmup)
     line = {"metric": METRIC, "value": cb["value"], "unit": cb["unit"], "n_gpus": rk.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_call"],

@@ -66,3 +66,20 @@ def test_partitioned_reduction_shards_are_near_equal():
     w = CONFIGS["reduce_f32_2p28p1"]
     sizes = [bench.local_workload(w, r, 8).shape[0] for r in range(8)]
     assert sum(sizes) == 2**28 + 1 and max(sizes) - min(sizes) == 1
+
+
+def test_reference_arm_reports_unavailable_without_the_package(tmp_path, monkeypatch, capsys):
+    import json
+
+    from kernelpilot_b200 import harness
+
+    monkeypatch.setenv("KP_REF_HARNESS", str(tmp_path))
+    harness.reference.cache_clear()
+    try:
+        args = type("A", (), {"workload": "reduce_f32_2p28p1", "steps": 1, "warmup": 3})()
+        assert bench.run_reference(args, bench.kdist.Rank(0, 1, 0)) == 0
+        line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+        assert line["impl"] == "reference" and "not installed" in line["unavailable"]
+    finally:
+        monkeypatch.delenv("KP_REF_HARNESS")
+        harness.reference.cache_clear()

@@ -12,9 +12,12 @@ CASES = [
     ("vector_add", (1_000_003,), torch.bfloat16),
     ("reduce_sum", (1_000_003,), torch.float32),
     ("softmax", (300, 4097), torch.float32),
+    ("softmax", (64, 131072), torch.bfloat16),      # thread-block clusters, DSMEM exchange
+    ("softmax", (7, 65537), torch.float32),         # clusters on unaligned rows
     ("layernorm", (300, 4097), torch.bfloat16),
-    ("matmul", (300, 4097, 192), torch.bfloat16),   # includes the pitch copy of B
-    ("matmul", (1024, 1024, 1024), torch.float16),
+    ("matmul", (300, 4097, 192), torch.bfloat16),   # pitch copy of B, then the CTA-pair GEMM (PDL)
+    ("matmul", (1024, 1024, 1024), torch.float16),  # CTA pairs (clusters of two)
+    ("matmul", (128, 1024, 512), torch.bfloat16),   # M <= 128: the one-CTA kernel
     ("attention", (1, 4, 1000, 128), torch.bfloat16),
     ("attention_causal", (1, 4, 1000, 128), torch.bfloat16),  # main + few-key grids (PDL)
 ]
