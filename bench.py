@@ -484,6 +484,37 @@ def triton_twins(w: Workload, inputs: tuple, peak: float) -> dict:
 
 # ------------------------------------------------------------------ the configs table
 
+def time_assemble(w: Workload, out: torch.Tensor, world: int) -> dict:
+    """The whole output gathered on every rank (``dist.assemble_rows``: one NCCL
+    all_gather of the row / (batch, head) / element blocks), the second call's
+    max-over-ranks device time. Not part of the sharded step: an op's outputs stay
+    sharded unless a caller asks for them whole."""
+    units = w.shape[0] * w.shape[1] if w.kernel in ("attention", "attention_causal") \
+        else w.shape[0]
+    if w.kernel in ("attention", "attention_causal"):
+        local = out.reshape(out.shape[1], -1)   # (1, B*H slices, S, D)
+    elif w.kernel == "vector_add":
+        local = out.reshape(-1, 1)
+    else:
+        local = out.reshape(out.shape[0], -1)   # rows
+    counts = kdist.row_counts(units, world)
+    del kdist.assemble_rows(local.contiguous(), counts)  # first call: NCCL set-up
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    full = kdist.assemble_rows(local.contiguous(), counts)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    got = full.numel() * full.element_size() - local.numel() * local.element_size()
+    del full
+    return {"ms": round(float(ms.item()), 4), "bytes_in_per_rank": got,
+            "GB_s_per_rank": round(got / (float(ms.item()) / 1e3) / 1e9, 1),
+            "how": "dist.assemble_rows: NCCL all_gather of the output blocks"}
+
+
 def measure_row(w: Workload, rk: kdist.Rank, with_host: bool, warmup: int = 3,
                 budget_ms: float = 5.0, min_steps: int = 10, max_steps: int = 50,
                 with_triton: bool = False) -> dict:
@@ -527,6 +558,8 @@ def measure_row(w: Workload, rk: kdist.Rank, with_host: bool, warmup: int = 3,
     torch.cuda.synchronize()
     if rk.rank == 0:
         row["check"] = rounded(spot_check(w, inputs, out), 8)
+    if world > 1 and w.kernel != "reduce_sum":
+        row["assemble"] = time_assemble(w, out, world)
     del out
     if with_triton and world == 1:
         row["triton_twins"] = triton_twins(w, inputs, peak)

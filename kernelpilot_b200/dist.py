@@ -248,10 +248,16 @@ class PeerSum:
 
 def assemble_rows(local: torch.Tensor, counts: list[int]) -> torch.Tensor:
     """All-gather row blocks of (possibly) unequal sizes into the full tensor along
-    dim 0, in rank order."""
+    dim 0, in rank order. Equal blocks are gathered straight into the result; unequal
+    ones are padded to the largest and compacted afterwards."""
     world = dist.get_world_size()
     if world == 1:
         return local
+    if all(c == counts[0] for c in counts):
+        out = torch.empty((counts[0] * world,) + tuple(local.shape[1:]), dtype=local.dtype,
+                          device=local.device)
+        dist.all_gather_into_tensor(out, local.contiguous())
+        return out
     cap = max(counts)
     pad = torch.zeros((cap - local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
                       device=local.device)

@@ -148,8 +148,10 @@ def _sharded_op_worker(rank, world, port, q):
 
         kdist.init(backend="gloo", timeout_s=30)
         ok = []
+        # unequal blocks (padded gather) and equal ones (gathered in place)
         for kernel, shape in [("softmax", (9, 33)), ("matmul", (9, 5, 7)),
-                              ("attention", (1, 3, 16, 8)), ("layernorm", (5, 12))]:
+                              ("attention", (1, 3, 16, 8)), ("layernorm", (5, 12)),
+                              ("softmax", (8, 33)), ("attention", (2, 2, 16, 8))]:
             spec = get_spec(kernel)
             full = spec.make_inputs(shape, torch.float32, torch.device("cpu"), 0)
             local = kdist.shard_inputs(kernel, full, rank, world)
@@ -179,4 +181,4 @@ def test_two_gloo_ranks_split_each_op_and_reassemble_its_output():
     for p in procs:
         p.join(timeout=60)
     for rank, ok in results:
-        assert ok == [True, True, True, True], (rank, ok)
+        assert ok == [True] * 6, (rank, ok)
