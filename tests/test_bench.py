@@ -83,3 +83,22 @@ def test_reference_arm_reports_unavailable_without_the_package(tmp_path, monkeyp
     finally:
         monkeypatch.delenv("KP_REF_HARNESS")
         harness.reference.cache_clear()
+
+
+@pytest.mark.parametrize("key,shape", [
+    ("softmax_f32_4096x4097", (70, 300)), ("gemm_bf16_8192", (80, 48, 64)),
+    ("attn_bf16_b8h32s4096d128", (1, 2, 64, 32)), ("vadd_f32_2p26", (5000,)),
+    ("layernorm_f32_8192x8192", (70, 200)), ("reduce_f32_2p28p1", (10001,))])
+def test_spot_check_passes_a_correct_output_and_catches_a_wrong_one(key, shape):
+    import dataclasses
+
+    import torch
+
+    w = dataclasses.replace(CONFIGS[key], shape=shape)
+    inputs = w.make_inputs(shape, w.dtype, torch.device("cpu"), 0)
+    out = w.spec.baseline(*inputs)
+    res = bench.spot_check(w, inputs, out)
+    assert res["ok"], res
+    bad = out.clone()
+    bad.reshape(-1)[0] += 1.0
+    assert not bench.spot_check(w, inputs, bad)["ok"]
