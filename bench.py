@@ -484,10 +484,12 @@ def triton_twins(w: Workload, inputs: tuple, peak: float) -> dict:
 
 # ------------------------------------------------------------------ the configs table
 
-def time_assemble(w: Workload, out: torch.Tensor, world: int) -> dict:
+def time_assemble(w: Workload, out: torch.Tensor, world: int, calls: int = 5) -> dict:
     """The whole output gathered on every rank (``dist.assemble_rows``: one NCCL
-    all_gather of the row / (batch, head) / element blocks), the second call's
-    max-over-ranks device time. Not part of the sharded step: an op's outputs stay
+    all_gather of the row / (batch, head) / element blocks): the median over
+    ``calls`` timed calls of each call's max-over-ranks device time, after two
+    untimed calls (the first in a process loads the copy kernels it uses and can take
+    milliseconds of host time). Not part of the sharded step: an op's outputs stay
     sharded unless a caller asks for them whole."""
     units = w.shape[0] * w.shape[1] if w.kernel in ("attention", "attention_causal") \
         else w.shape[0]
@@ -497,21 +499,27 @@ def time_assemble(w: Workload, out: torch.Tensor, world: int) -> dict:
         local = out.reshape(-1, 1)
     else:
         local = out.reshape(out.shape[0], -1)   # rows
+    local = local.contiguous()
     counts = kdist.row_counts(units, world)
-    kdist.assemble_rows(local.contiguous(), counts)  # first call: NCCL set-up (untimed)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.distributed.barrier()
-    torch.cuda.synchronize()
-    e0.record()
-    full = kdist.assemble_rows(local.contiguous(), counts)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    for _ in range(2):
+        kdist.assemble_rows(local, counts)      # untimed
+    per_call = []
+    for _ in range(calls):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        full = kdist.assemble_rows(local, counts)
+        e1.record()
+        torch.cuda.synchronize()
+        got = full.numel() * full.element_size() - local.numel() * local.element_size()
+        del full
+        per_call.append(e0.elapsed_time(e1))
+    ms = torch.tensor(per_call, dtype=torch.float64, device="cuda")
     torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    got = full.numel() * full.element_size() - local.numel() * local.element_size()
-    del full
-    return {"ms": round(float(ms.item()), 4), "bytes_in_per_rank": got,
-            "GB_s_per_rank": round(got / (float(ms.item()) / 1e3) / 1e9, 1),
+    med = float(ms.median().item())
+    return {"ms": round(med, 4), "ms_calls": [round(float(v), 4) for v in ms.tolist()],
+            "bytes_in_per_rank": got, "GB_s_per_rank": round(got / (med / 1e3) / 1e9, 1),
             "how": "dist.assemble_rows: NCCL all_gather of the output blocks"}
 
 

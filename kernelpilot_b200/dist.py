@@ -246,26 +246,37 @@ class PeerSum:
         self._ps = None
 
 
+_GATHER_ALIGN = 256  # bytes per rank slot of a gathered block
+
+
 def assemble_rows(local: torch.Tensor, counts: list[int]) -> torch.Tensor:
     """All-gather row blocks of (possibly) unequal sizes into the full tensor along
-    dim 0, in rank order. Equal blocks are gathered straight into the result; unequal
-    ones are padded to the largest and compacted afterwards."""
+    dim 0, in rank order. Blocks of equal size whose bytes are a multiple of
+    ``_GATHER_ALIGN`` are gathered straight into the result. Any other blocks go
+    through one flat buffer whose per-rank slot is the largest block rounded up to
+    ``_GATHER_ALIGN`` bytes, and are compacted afterwards: NCCL moves misaligned
+    per-rank chunks at a small fraction of its aligned rate."""
     world = dist.get_world_size()
     if world == 1:
         return local
-    if all(c == counts[0] for c in counts):
-        out = torch.empty((counts[0] * world,) + tuple(local.shape[1:]), dtype=local.dtype,
-                          device=local.device)
-        dist.all_gather_into_tensor(out, local.contiguous())
+    local = local.contiguous()
+    inner = tuple(local.shape[1:])
+    row = 1
+    for d in inner:
+        row *= d
+    esize = local.element_size()
+    if all(c == counts[0] for c in counts) and (counts[0] * row * esize) % _GATHER_ALIGN == 0:
+        out = torch.empty((counts[0] * world,) + inner, dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(out, local)
         return out
-    cap = max(counts)
-    pad = torch.zeros((cap - local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
-                      device=local.device)
-    mine = torch.cat([local, pad]) if pad.shape[0] else local.contiguous()
-    out = torch.empty((cap * world,) + tuple(local.shape[1:]), dtype=local.dtype,
-                      device=local.device)
-    dist.all_gather_into_tensor(out, mine)
-    return torch.cat([out[i * cap: i * cap + c] for i, c in enumerate(counts)])
+    align = max(1, _GATHER_ALIGN // esize)
+    slot = -(-max(counts) * row // align) * align
+    mine = torch.zeros(slot, dtype=local.dtype, device=local.device)
+    mine[: local.numel()].copy_(local.reshape(-1))
+    flat = torch.empty(slot * world, dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(flat, mine)
+    return torch.cat([flat[i * slot: i * slot + c * row] for i, c in enumerate(counts)]
+                     ).reshape((sum(counts),) + inner)
 
 
 def row_counts(n: int, world: int) -> list[int]:

@@ -47,8 +47,16 @@ def _worker(rank, world, port, q):
         ra, rb = kdist.shard_range(7, rank, world)
         full = kdist.assemble_rows(torch.softmax(rows[ra:rb], -1),
                                    kdist.row_counts(7, world))
-        q.put((rank, float(total), float(x.double().sum()),
-               bool(torch.allclose(full, torch.softmax(rows, -1)))))
+        ok = bool(torch.allclose(full, torch.softmax(rows, -1)))
+        # equal blocks both sides of the slot alignment, and a 2-byte type unequal
+        for n_rows, width, dt in [(8, 3, torch.float32), (8, 32, torch.float32),
+                                  (9, 5, torch.bfloat16)]:
+            whole = torch.arange(n_rows * width, dtype=torch.float32).reshape(n_rows, width)
+            whole = whole.to(dt)
+            ra, rb = kdist.shard_range(n_rows, rank, world)
+            got = kdist.assemble_rows(whole[ra:rb], kdist.row_counts(n_rows, world))
+            ok = ok and got.dtype == dt and torch.equal(got, whole)
+        q.put((rank, float(total), float(x.double().sum()), ok))
         dist.destroy_process_group()
     except Exception as e:  # reported to the parent, which fails the test
         q.put((rank, "error", repr(e), False))
