@@ -128,6 +128,10 @@ EDGE = [
     # A rows not 16-byte aligned (K % 8 = 7): A staged alone, then A and B both staged
     ("matmul", (256, 512, 999), torch.float16),
     ("matmul", (300, 500, 1001), torch.bfloat16),
+    # B rows not 16-byte aligned with one 128-row block (pitch copy of B) and with a
+    # ragged K under several pair-tile waves (B rows staged by the GEMM itself)
+    ("matmul", (100, 4097, 300), torch.bfloat16),
+    ("matmul", (640, 3001, 1000), torch.float16),
     ("attention", (2, 3, 300, 128), torch.bfloat16),
     ("attention", (1, 4, 513, 64), torch.float16),
     ("attention_causal", (2, 3, 300, 128), torch.bfloat16),
