@@ -16,7 +16,10 @@ need no exchange (an all_gather would only assemble outputs).
 value      whole-job algorithmic bytes (or FLOPs) / max-over-ranks device time, inputs
            resident in HBM; per-step CUDA events; when a rank's working set is under
            twice the L2, L2 is flushed between steps outside the events (256 MB
-           written, then read back so no dirty lines are left for the timed kernel).
+           written, then read back so no dirty lines are left for the timed kernel;
+           for the reduction at N > 1 a one-element NCCL all_reduce after the flush
+           re-aligns the ranks, whose in-kernel exchange would otherwise time the
+           flushes' skew).
 e2e        the same metric through the public API (torch.ops.kp, and the peer-sum
            object at N > 1) with each rank's inputs copied from pinned host memory and
            the result copied back inside the timed region.
@@ -240,11 +243,15 @@ def time_steps(step, steps: int, flush: bool, world: int, align: bool = False
     would carry that launch skew (up to ~0.25 ms at N = 4). The stream first idles
     ~0.1 ms on the GPU, so the host can queue everything behind it, then runs one
     untimed step that brings the ranks together on the device; the timed steps
-    follow it back to back."""
+    follow it back to back. When the L2 is flushed between steps, each rank's flush
+    ends at its own time, so an aligned step is also preceded by a one-element NCCL
+    all_reduce (outside the timed region) that brings the ranks' streams together
+    again before the idle work that lets the hosts queue the step."""
     from kernelpilot_b200.harness import flush_l2
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    rejoin = torch.zeros(1, device="cuda") if align and world > 1 else None
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -254,6 +261,8 @@ def time_steps(step, steps: int, flush: bool, world: int, align: bool = False
     for i in range(steps):
         if flush:
             flush_l2(clean=True)
+            if rejoin is not None:
+                torch.distributed.all_reduce(rejoin)
             # ~50 us of GPU-side idle work after the flush, outside the timed region, so
             # the start event, the step and the end event are already queued when the GPU
             # reaches them (a late host would otherwise be timed as an idle gap)
@@ -721,8 +730,11 @@ def main() -> int:
         "higher_is_better": True, "scaling": "strong" if rk.world > 1 else "weak",
         "vs_baseline": None, "dtype": DTYPE_NAMES[w.dtype], "data": "synthetic",
         "config": job_config(w, rk.world),
-        "timing": {"l2": "flushed between steps outside the events (256 MB written, then "
-                         "read so no dirty lines remain)" if flush else
+        "timing": {"l2": ("flushed between steps outside the events (256 MB written, then "
+                          "read so no dirty lines remain)"
+                          + ("; then a one-element NCCL all_reduce re-aligns the ranks "
+                             "before the next step" if isinstance(exchange, kdist.PeerSum)
+                             else "")) if flush else
                    "each rank's inputs larger than twice the L2",
                    "exchange": exchange_desc,
                    "ranks": "max over ranks of the summed per-step CUDA-event times"},
