@@ -387,6 +387,19 @@ def cpu_sample(w: Workload) -> tuple[tuple, float, str]:
     return (q, k, v), 1.0 / (B * H), f"1 of {B * H} (batch, head) slices"
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (Linux /proc/cpuinfo), or the platform's processor."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
 def time_cpu(w: Workload, reps: int, budget_s: float = 20.0) -> dict:
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
@@ -404,6 +417,7 @@ def time_cpu(w: Workload, reps: int, budget_s: float = 20.0) -> dict:
     sec = statistics.median(times) / frac  # scaled to one full call
     value = work_per_call(w) / sec / 1e12
     return {"value": value, "unit": unit_of(w), "cores": torch.get_num_threads(),
+            "cpu_model": cpu_model(),
             "kind": kind, "sample": f"{label}, median of {len(times)} calls, "
                                    f"scaled to one full call",
             "ms_per_call": sec * 1e3}

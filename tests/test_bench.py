@@ -102,3 +102,13 @@ def test_spot_check_passes_a_correct_output_and_catches_a_wrong_one(key, shape):
     bad = out.clone()
     bad.reshape(-1)[0] += 1.0
     assert not bench.spot_check(w, inputs, bad)["ok"]
+
+
+def test_cpu_baseline_names_its_cores_and_model():
+    # the reference's CPU path on a small vector: the record carries what it ran on
+    import bench
+    w = bench.CONFIGS["reduce_f32_2p28p1"]
+    rec = bench.time_cpu(w, reps=1, budget_s=1.0)
+    assert rec["cores"] >= 1 and rec["kind"] in ("reference", "port")
+    assert isinstance(rec["cpu_model"], str) and rec["cpu_model"]
+    assert rec["value"] > 0 and rec["unit"] == "TB/s"
