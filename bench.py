@@ -233,6 +233,20 @@ def make_step(w: Workload, inputs: tuple, exchange=None):
     return lambda: fn(*inputs)
 
 
+def decide_flush(inputs: tuple, world: int) -> bool:
+    """Flush L2 between steps when this job's inputs would otherwise stay in it: the
+    largest rank's input bytes under twice the L2. Decided from the max over ranks, so
+    every rank takes the same steps (the flush of an exchanging step is followed by a
+    collective)."""
+    nbytes = sum(t.numel() * t.element_size() for t in inputs)
+    if world > 1:
+        t = torch.tensor([float(nbytes)], dtype=torch.float64,
+                         device=inputs[0].device if inputs else "cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        nbytes = int(t.item())
+    return nbytes < 2 * L2_BYTES
+
+
 def time_steps(step, steps: int, flush: bool, world: int, align: bool = False
                ) -> tuple[float, list[float]]:
     """(max-over-ranks total ms of the K steps, per-step ms on this rank).
@@ -573,7 +587,7 @@ def measure_row(w: Workload, rk: kdist.Rank, with_host: bool, warmup: int = 3,
     if world > 1:  # every rank must time the same number of calls
         torch.distributed.all_reduce(est, op=torch.distributed.ReduceOp.MAX)
     steps = int(min(max_steps, max(min_steps, budget_ms / float(est.item()))))
-    flush = sum(t.numel() * t.element_size() for t in inputs) < 2 * L2_BYTES
+    flush = decide_flush(inputs, world)
     total, per = time_steps(step, steps, flush, world, align=isinstance(exchange, kdist.PeerSum))
     ms = total / steps
     peak, src = roofline_peak(w)
@@ -645,8 +659,7 @@ def main() -> int:
     lw = local_workload(w, rk.rank, rk.world)
     inputs = kdist.shard_inputs(w.kernel, w.inputs("cuda", seed=0), rk.rank, rk.world)
     torch.cuda.empty_cache()
-    in_bytes = sum(t.numel() * t.element_size() for t in inputs)
-    flush = in_bytes < 2 * L2_BYTES
+    flush = decide_flush(inputs, rk.world)
     exchange, exchange_desc = (None, "none")
     if w.kernel == "reduce_sum":
         exchange, exchange_desc = (reduce_exchange(rk) if rk.world > 1

@@ -112,3 +112,41 @@ def test_cpu_baseline_names_its_cores_and_model():
     assert rec["cores"] >= 1 and rec["kind"] in ("reference", "port")
     assert isinstance(rec["cpu_model"], str) and rec["cpu_model"]
     assert rec["value"] > 0 and rec["unit"] == "TB/s"
+
+
+def _flush_worker(rank, world, port, q):
+    import os
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    try:
+        import torch
+        import torch.distributed as dist
+
+        import bench
+        from kernelpilot_b200 import dist as kdist
+        kdist.init(backend="gloo", timeout_s=30)
+        bench.L2_BYTES = 1000  # shards of 1996 and 2004 bytes straddle 2 x L2
+        x = torch.zeros(499 if rank == 0 else 501)
+        q.put((rank, bench.decide_flush((x,), world)))
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e)))
+
+
+def test_flush_decision_is_the_same_on_every_rank():
+    # a rank-local decision could send one rank into the post-flush collective alone
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_flush_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert got[0] is False and got[1] is False, got  # the larger shard decides
