@@ -57,9 +57,7 @@ sys.path.insert(0, str(REPO))
 from kernelpilot_b200 import dist as kdist  # noqa: E402
 from kernelpilot_b200.specs import CONFIGS, Workload  # noqa: E402
 
-METRIC = json.loads((REPO / "BASELINE.json").read_text())["metric"] \
-    if (REPO / "BASELINE.json").exists() else \
-    "achieved HBM TB/s (softmax/reduce) and BF16 TFLOPS (GEMM/attn), % of peak"
+METRIC = "achieved HBM TB/s (softmax/reduce) and BF16 TFLOPS (GEMM/attn), % of peak"
 DEFAULT_WORKLOAD = "reduce_f32_2p28p1"
 L2_BYTES = 126 * 1024 * 1024
 DTYPE_NAMES = {torch.float32: "f32", torch.float16: "f16", torch.bfloat16: "bf16"}
