@@ -3,8 +3,8 @@ reference's op semantics and of its correctness comparator.
 
 TEST INFRASTRUCTURE ONLY. Nothing in the product path imports this module: it is
 used by tests/, by ``__graft_entry__.smoke()`` and by bench.py's ``cpu_baseline`` /
-reference arm, and only ever as the checker or the CPU baseline, never as the thing
-measured or shipped.
+reference arm, and only ever as the reference results are compared against or as the
+CPU baseline, never as the thing measured or shipped.
 
 Pinned against the reference itself: tests/golden/make_golden.py imports the
 reference package (kernelpilot/specs.py), generates seeded inputs with its own
