@@ -275,10 +275,12 @@ def time_steps(step, steps: int, flush: bool, world: int, align: bool = False
             flush_l2(clean=True)
             if rejoin is not None:
                 torch.distributed.all_reduce(rejoin)
-            # ~50 us of GPU-side idle work after the flush, outside the timed region, so
-            # the start event, the step and the end event are already queued when the GPU
-            # reaches them (a late host would otherwise be timed as an idle gap)
-            torch.cuda._sleep(100_000)
+            # GPU-side idle work after the flush, outside the timed region, so the start
+            # event, the step and the end event are already queued when the GPU reaches
+            # them (a late host would otherwise be timed as an idle gap): ~50 us, or
+            # ~0.5 ms after a re-alignment, where one rank's late host would also be
+            # timed by every other rank's exchange
+            torch.cuda._sleep(100_000 if rejoin is None else 1_000_000)
         starts[i].record()
         step()
         ends[i].record()
