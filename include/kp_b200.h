@@ -63,9 +63,9 @@ int kpb_vector_add(int variant, int dtype, const void* a, const void* b, void* c
  * out[0] = sum of x[0..n) accumulated in fp32. Unlike the reference, `out` need not
  * be zero-initialised: it is overwritten (a zeroed `out` gives the same result).
  * The result is deterministic: per-CTA partials are combined in a fixed order.
- * kpb_reduce_sum takes its partials buffer from the stream-ordered CUDA allocator
- * (cudaMallocAsync/cudaFreeAsync on `stream`); kpb_reduce_sum_ws takes it from the
- * caller instead. */
+ * kpb_reduce_sum takes its partials buffer from a stream-ordered pool the library
+ * keeps per device (allocated and freed on `stream`; the pool keeps its memory
+ * between calls); kpb_reduce_sum_ws takes it from the caller instead. */
 int kpb_reduce_sum(int variant, int dtype, const void* x, float* out, int64_t n,
                    void* stream);
 size_t kpb_reduce_sum_workspace_bytes(int variant, int64_t n);
@@ -125,7 +125,7 @@ int kpb_softmax(int variant, int dtype, const void* x, void* y, int64_t M, int64
  * C = A @ B, row-major A (M, K), B (K, N), C (M, N); fp32 accumulation, output in
  * the input dtype; K == 0 writes zeros. kpb_matmul obtains any staging buffer it
  * needs (a 16-byte-aligned copy of B when N*elem is not a multiple of 16) from
- * the stream-ordered allocator; kpb_matmul_ws takes it from the caller. */
+ * the library's stream-ordered pool; kpb_matmul_ws takes it from the caller. */
 int kpb_matmul(int variant, int dtype, const void* A, const void* B, void* C, int64_t M,
                int64_t N, int64_t K, void* stream);
 size_t kpb_matmul_workspace_bytes(int variant, int dtype, int64_t M, int64_t N, int64_t K);

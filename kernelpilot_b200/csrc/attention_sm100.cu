@@ -492,7 +492,7 @@ int launch_attn(const T* q, const T* k, const T* v, T* o, int64_t BH, int64_t S,
   if (n_ct > n_split) {
     // causal: heaviest blocks first
     auto kern = attn_fwd_tc<T, D, kCausal, false>;
-    KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if (int rc = ensure_dyn_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
     const dim3 grid(static_cast<unsigned>(n_ct - n_split), static_cast<unsigned>(BH));
     kern<<<grid, kThreads, smem, s>>>(mq, mk, mv, o, static_cast<int>(S), scale_log2,
                                       kCausal ? n_ct - 1 : n_split, kCausal ? -1 : 1, err);
@@ -500,7 +500,7 @@ int launch_attn(const T* q, const T* k, const T* v, T* o, int64_t BH, int64_t S,
   }
   if (n_split > 0) {
     auto kern = attn_fwd_tc<T, D, kCausal, true>;
-    KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if (int rc = ensure_dyn_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(n_split), static_cast<unsigned>(BH));
     cfg.blockDim = dim3(kThreads);

@@ -1,8 +1,10 @@
 // The extern "C" boundary (include/kp_b200.h): argument validation, status codes,
-// per-thread error messages, stream-ordered scratch, and the per-device error word
-// that bounded waits inside kernels report timeouts to.
+// per-thread error messages, stream-ordered scratch from a pool of its own, and the
+// per-device error word that bounded waits inside kernels report timeouts to.
+#include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 
 #include "kp_common.cuh"
 
@@ -61,6 +63,98 @@ int sm_count() {
     g_sms[dev] = n;
   }
   return g_sms[dev];
+}
+
+// Scratch of the allocating entry points comes from a stream-ordered pool per device
+// owned by this library, which keeps its memory between calls (release threshold
+// unlimited). The device's default pool returns its memory at every synchronisation,
+// so the next call would map it again on the host after the GPU had already reached
+// the call, and the GPU would wait for it.
+namespace {
+cudaMemPool_t g_pool[kMaxDevices] = {};
+}  // namespace
+
+int scratch_alloc(void** p, size_t bytes, cudaStream_t s) {
+  int dev = 0;
+  KPB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(KPB_EUNSUPPORTED, "device index out of range");
+  cudaMemPool_t pool = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_pool[dev] == nullptr) {
+      cudaMemPoolProps props = {};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      cudaMemPool_t created = nullptr;
+      KPB_CUDA(cudaMemPoolCreate(&created, &props));
+      uint64_t keep = UINT64_MAX;
+      const cudaError_t e = cudaMemPoolSetAttribute(created, cudaMemPoolAttrReleaseThreshold, &keep);
+      if (e != cudaSuccess) {
+        cudaMemPoolDestroy(created);
+        return cuda_fail(e, "cudaMemPoolSetAttribute", __FILE__, __LINE__);
+      }
+      g_pool[dev] = created;
+    }
+    pool = g_pool[dev];
+  }
+  KPB_CUDA(cudaMallocFromPoolAsync(p, bytes, pool, s));
+  return KPB_OK;
+}
+
+// Launch facts of a kernel that do not change within a process, per device: the
+// dynamic shared-memory opt-in is set once, and occupancy answers are kept. The
+// runtime queries cost tens to hundreds of microseconds of host time per call.
+namespace {
+using LaunchKey = std::tuple<int, const void*, int, size_t, int>;
+std::map<LaunchKey, int> g_launch_facts;
+
+int current_device(int* dev) {
+  KPB_CUDA(cudaGetDevice(dev));
+  return KPB_OK;
+}
+}  // namespace
+
+int ensure_dyn_smem(const void* func, int bytes) {
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  const LaunchKey key{dev, func, -1, static_cast<size_t>(bytes), 0};
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_launch_facts.count(key)) return KPB_OK;
+  KPB_CUDA(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  g_launch_facts[key] = 1;
+  return KPB_OK;
+}
+
+int occupancy_blocks(const void* func, int threads, size_t smem, int* out) {
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  const LaunchKey key{dev, func, threads, smem, 1};
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_launch_facts.find(key);
+  if (it == g_launch_facts.end()) {
+    int occ = 0;
+    KPB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, func, threads, smem));
+    it = g_launch_facts.emplace(key, occ).first;
+  }
+  *out = it->second;
+  return KPB_OK;
+}
+
+int occupancy_clusters(const void* func, const cudaLaunchConfig_t& cfg, int cluster, int* out) {
+  int dev = 0;
+  if (int rc = current_device(&dev)) return rc;
+  const LaunchKey key{dev, func, static_cast<int>(cfg.blockDim.x), cfg.dynamicSmemBytes,
+                      100 + cluster};
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_launch_facts.find(key);
+  if (it == g_launch_facts.end()) {
+    int active = 0;
+    KPB_CUDA(cudaOccupancyMaxActiveClusters(&active, func, &cfg));
+    it = g_launch_facts.emplace(key, active).first;
+  }
+  *out = it->second;
+  return KPB_OK;
 }
 
 // Device address of this device's error word (looked up once per device).
@@ -154,7 +248,8 @@ int kpb_reduce_sum(int variant, int dtype, const void* x, float* out, int64_t n,
   auto s = static_cast<cudaStream_t>(stream);
   const size_t bytes = reduce_workspace_bytes(variant, n);
   void* ws = nullptr;
-  if (bytes) KPB_CUDA(cudaMallocAsync(&ws, bytes, s));
+  if (bytes)
+    if (int rc = scratch_alloc(&ws, bytes, s)) return rc;
   const int rc = reduce_sum(variant, dtype, x, out, n, ws, bytes, s);
   if (ws) {
     const cudaError_t e = cudaFreeAsync(ws, s);
@@ -219,7 +314,8 @@ int kpb_matmul(int variant, int dtype, const void* A, const void* B, void* C, in
   auto s = static_cast<cudaStream_t>(stream);
   const size_t bytes = matmul_workspace_bytes(variant, dtype, M, N, K);
   void* ws = nullptr;
-  if (bytes) KPB_CUDA(cudaMallocAsync(&ws, bytes, s));
+  if (bytes)
+    if (int rc = scratch_alloc(&ws, bytes, s)) return rc;
   const int rc = kpb_matmul_ws(variant, dtype, A, B, C, M, N, K, ws, bytes, stream);
   if (ws) {
     const std::string msg = g_last_error;

@@ -31,6 +31,12 @@ int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t err, const char* what, const char* file, int line);
 // SM count of the current device (cached per device).
 int sm_count();
+// Per-device, per-kernel launch facts, queried once (capi.cu): the dynamic
+// shared-memory opt-in, and the occupancy of a block size / shared-memory size /
+// cluster size (cfg's grid is not part of the answer).
+int ensure_dyn_smem(const void* func, int bytes);
+int occupancy_blocks(const void* func, int threads, size_t smem, int* out);
+int occupancy_clusters(const void* func, const cudaLaunchConfig_t& cfg, int cluster, int* out);
 
 #define KPB_CUDA(call)                                                   \
   do {                                                                   \

@@ -440,11 +440,15 @@ gemm_tc_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CU
 }
 
 // dst (rows x cols_pad) = src (rows x cols) with zero columns appended; cols_pad is a
-// multiple of 8, so every thread writes one aligned 16-byte vector of a dst row
-// (coalesced 2-byte reads of the unaligned source row).
+// multiple of 8, so every thread writes aligned 16-byte vectors of a dst row.
 // Interior vectors read the two aligned 16-byte words that cover them and shift the
 // row's 2-byte misalignment out with funnel shifts; vectors at row or buffer ends
-// fall back to masked 2-byte loads.
+// fall back to masked 2-byte loads. A CTA of kPadThreads takes whole rows (rows
+// blockIdx.x, + gridDim.x, ...), and each thread issues the loads of kPadUnroll
+// vectors before it stores any, so a row's loads are in flight together.
+constexpr int kPadThreads = 128;
+constexpr int kPadUnroll = 4;
+
 __device__ __forceinline__ uint32_t word_at(const uint4& a, const uint4& b, int i) {
   switch (i) {
     case 0: return a.x; case 1: return a.y; case 2: return a.z; case 3: return a.w;
@@ -453,41 +457,55 @@ __device__ __forceinline__ uint32_t word_at(const uint4& a, const uint4& b, int 
 }
 
 template <typename T>
-__global__ void pad_cols(const T* __restrict__ src, T* __restrict__ dst, int64_t rows,
-                         int64_t cols, int64_t cols_pad) {
+__global__ void __launch_bounds__(kPadThreads)
+pad_cols(const T* __restrict__ src, T* __restrict__ dst, int64_t rows, int64_t cols,
+         int64_t cols_pad) {
   // the GEMM that reads dst may launch now; its loads wait for this grid to finish
   pdl_launch_dependents();
   const int64_t nvec = cols_pad / 8;
   const uintptr_t src_lo = reinterpret_cast<uintptr_t>(src);
   const uintptr_t src_hi = src_lo + static_cast<uintptr_t>(rows * cols) * 2;
-  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const T* s = src + r * cols;
     uint4* d = reinterpret_cast<uint4*>(dst + r * cols_pad);
     const uintptr_t rs = reinterpret_cast<uintptr_t>(s);
     const uintptr_t base = rs & ~uintptr_t(15);
     const int off = static_cast<int>(rs - base);  // even, 0..14
-    for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
-         v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-      const uintptr_t w0 = base + static_cast<uintptr_t>(v) * 16;
-      if (v * 8 + 8 <= cols && w0 >= src_lo && w0 + 32 <= src_hi) {
-        const uint4 a = *reinterpret_cast<const uint4*>(w0);
-        const uint4 b = *reinterpret_cast<const uint4*>(w0 + 16);
-        const int q = off >> 2, sh = (off & 3) * 8;
-        uint32_t o[4];
+    const int q = off >> 2, sh = (off & 3) * 8;
+    for (int64_t v0 = threadIdx.x; v0 < nvec; v0 += kPadUnroll * kPadThreads) {
+      uint4 lo[kPadUnroll], hi[kPadUnroll];
+      bool fast[kPadUnroll];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o[i] = __funnelshift_r(word_at(a, b, q + i), word_at(a, b, q + i + 1), sh);
-        d[v] = make_uint4(o[0], o[1], o[2], o[3]);
-        continue;
+      for (int k = 0; k < kPadUnroll; ++k) {
+        const int64_t v = v0 + k * kPadThreads;
+        const uintptr_t w0 = base + static_cast<uintptr_t>(v) * 16;
+        fast[k] = v < nvec && v * 8 + 8 <= cols && w0 >= src_lo && w0 + 32 <= src_hi;
+        if (fast[k]) {
+          lo[k] = *reinterpret_cast<const uint4*>(w0);
+          hi[k] = *reinterpret_cast<const uint4*>(w0 + 16);
+        }
       }
-      uint16_t e[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int64_t c = v * 8 + i;
-        e[i] = c < cols ? reinterpret_cast<const uint16_t*>(s)[c] : uint16_t(0);
+      for (int k = 0; k < kPadUnroll; ++k) {
+        const int64_t v = v0 + k * kPadThreads;
+        if (v >= nvec) continue;
+        if (fast[k]) {
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o[i] = __funnelshift_r(word_at(lo[k], hi[k], q + i), word_at(lo[k], hi[k], q + i + 1), sh);
+          d[v] = make_uint4(o[0], o[1], o[2], o[3]);
+        } else {
+          uint16_t e[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int64_t c = v * 8 + i;
+            e[i] = c < cols ? reinterpret_cast<const uint16_t*>(s)[c] : uint16_t(0);
+          }
+          d[v] = make_uint4(e[0] | (uint32_t(e[1]) << 16), e[2] | (uint32_t(e[3]) << 16),
+                            e[4] | (uint32_t(e[5]) << 16), e[6] | (uint32_t(e[7]) << 16));
+        }
       }
-      d[v] = make_uint4(e[0] | (uint32_t(e[1]) << 16), e[2] | (uint32_t(e[3]) << 16),
-                        e[4] | (uint32_t(e[5]) << 16), e[6] | (uint32_t(e[7]) << 16));
     }
   }
 }
@@ -533,7 +551,7 @@ int launch_tc(const T* A, const T* B, T* C, int64_t M, int64_t N, int64_t K, voi
   const int sms = sm_count();
   if (st.pad_a) {
     T* ap = reinterpret_cast<T*>(w);
-    pad_cols<T><<<dim3(static_cast<unsigned>(cdiv(st.kp / 8, 256)), static_cast<unsigned>(std::min<int64_t>(M, 8192))), 256, 0, s>>>(A, ap, M, K, st.kp);
+    pad_cols<T><<<static_cast<unsigned>(std::min<int64_t>(M, 1 << 16)), kPadThreads, 0, s>>>(A, ap, M, K, st.kp);
     KPB_LAUNCHED("matmul pad A");
     a = ap;
     lda = st.kp;
@@ -541,7 +559,7 @@ int launch_tc(const T* A, const T* B, T* C, int64_t M, int64_t N, int64_t K, voi
   }
   if (st.pad_b) {
     T* bp = reinterpret_cast<T*>(w);
-    pad_cols<T><<<dim3(static_cast<unsigned>(cdiv(st.np / 8, 256)), static_cast<unsigned>(std::min<int64_t>(K, 8192))), 256, 0, s>>>(B, bp, K, N, st.np);
+    pad_cols<T><<<static_cast<unsigned>(std::min<int64_t>(K, 1 << 16)), kPadThreads, 0, s>>>(B, bp, K, N, st.np);
     KPB_LAUNCHED("matmul pad B");
     b = bp;
     ldb = st.np;
@@ -553,8 +571,7 @@ int launch_tc(const T* A, const T* B, T* C, int64_t M, int64_t N, int64_t K, voi
   // with a padded A the K loop runs over the zero-padded width (B reads zeros there)
   if (M > BM) {
     auto kern = gemm_tc_pair<T>;
-    KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  kPairSmemBytes));
+    if (int rc = ensure_dyn_smem(reinterpret_cast<const void*>(kern), kPairSmemBytes)) return rc;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -570,7 +587,7 @@ int launch_tc(const T* A, const T* B, T* C, int64_t M, int64_t N, int64_t K, voi
     cfg.stream = s;
     cfg.gridDim = dim3(static_cast<unsigned>(sms / 2 * 2));
     int active = 0;
-    KPB_CUDA(cudaOccupancyMaxActiveClusters(&active, kern, &cfg));
+    if (int rc = occupancy_clusters(reinterpret_cast<const void*>(kern), cfg, 2, &active)) return rc;
     if (active < 1) return fail(KPB_ECUDA, "matmul: the CTA-pair kernel does not fit");
     const int64_t pair_tiles = cdiv(M, kPairBM) * cdiv(N, kPairBN);
     const int64_t pairs = std::min<int64_t>(pair_tiles, active);
@@ -580,7 +597,7 @@ int launch_tc(const T* A, const T* B, T* C, int64_t M, int64_t N, int64_t K, voi
     return KPB_OK;
   }
   auto kern = gemm_tc<T>;
-  KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  if (int rc = ensure_dyn_smem(reinterpret_cast<const void*>(kern), kSmemBytes)) return rc;
   const int64_t tiles = cdiv(M, BM) * cdiv(N, BN);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];

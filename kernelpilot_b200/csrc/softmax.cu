@@ -661,10 +661,10 @@ int launch_staged(const T* x, T* y, int64_t M, int64_t N, const StagedPlan& p, u
                   cudaStream_t s) {
   auto kern = softmax_staged<T, V, kAligned>;
   const size_t smem = 128 + size_t(p.stages) * p.stage_bytes;
-  KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(smem)));
+  const void* fn = reinterpret_cast<const void*>(kern);
+  if (int rc = ensure_dyn_smem(fn, static_cast<int>(smem))) return rc;
   int occ = 0;
-  KPB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, p.threads, smem));
+  if (int rc = occupancy_blocks(fn, p.threads, smem, &occ)) return rc;
   if (occ < 1) return fail(KPB_ECUDA, "softmax: staged kernel does not fit on an SM");
   const int64_t grid = std::min<int64_t>(M, int64_t(sm_count()) * std::min(occ, p.ctas_per_sm));
   kern<<<static_cast<unsigned>(grid), p.threads, smem, s>>>(x, y, M, static_cast<int>(N),
@@ -692,8 +692,8 @@ int launch_cluster(const T* x, T* y, int64_t M, int64_t N, int C, int nvc, const
                    unsigned* err, cudaStream_t s) {
   auto kern = softmax_cluster<T, V, kAligned>;
   const size_t smem = 128 + size_t(p.stages) * p.stage_bytes;
-  KPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(smem)));
+  if (int rc = ensure_dyn_smem(reinterpret_cast<const void*>(kern), static_cast<int>(smem)))
+    return rc;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -708,7 +708,7 @@ int launch_cluster(const T* x, T* y, int64_t M, int64_t N, int C, int nvc, const
   // as many clusters as can be resident at once (at most one per row)
   cfg.gridDim = dim3(static_cast<unsigned>(C * sm_count()));
   int active = 0;
-  KPB_CUDA(cudaOccupancyMaxActiveClusters(&active, kern, &cfg));
+  if (int rc = occupancy_clusters(reinterpret_cast<const void*>(kern), cfg, C, &active)) return rc;
   if (active < 1) return fail(KPB_ECUDA, "softmax: cluster kernel does not fit");
   const int64_t clusters = std::min<int64_t>(M, active);
   cfg.gridDim = dim3(static_cast<unsigned>(clusters * C));
