@@ -115,14 +115,17 @@ int current_device(int* dev) {
 }
 }  // namespace
 
+// The opt-in is one value per kernel and device, and a launch may use any amount up
+// to it: it is only ever raised, to the largest amount asked for so far.
 int ensure_dyn_smem(const void* func, int bytes) {
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
-  const LaunchKey key{dev, func, -1, static_cast<size_t>(bytes), 0};
+  const LaunchKey key{dev, func, -1, 0, 0};
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_launch_facts.count(key)) return KPB_OK;
+  auto it = g_launch_facts.find(key);
+  if (it != g_launch_facts.end() && it->second >= bytes) return KPB_OK;
   KPB_CUDA(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  g_launch_facts[key] = 1;
+  g_launch_facts[key] = bytes;
   return KPB_OK;
 }
 

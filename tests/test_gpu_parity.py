@@ -327,3 +327,14 @@ def test_no_kernel_wait_timed_out():
     bits = ctypes.c_uint(0)
     ext.capi_check(lib.kpb_device_errors(ctypes.byref(bits)))
     assert bits.value == 0
+
+
+@pytest.mark.gpu
+def test_kernel_attributes_survive_smaller_launches_in_between():
+    # the dynamic shared-memory opt-in of a kernel is one value: a launch asking for
+    # less must not lower it under what an earlier, larger launch needed
+    spec = get_spec("softmax")
+    fn = registry.best("softmax")
+    for shape in [(4, 32768), (4, 1024), (4, 32768), (300, 4095), (4, 32768)]:
+        res = check_impl(spec, "best", fn, shape, torch.bfloat16, "cuda")
+        assert res.ok, res.summary()
