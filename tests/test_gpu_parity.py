@@ -335,6 +335,9 @@ def test_kernel_attributes_survive_smaller_launches_in_between():
     # less must not lower it under what an earlier, larger launch needed
     spec = get_spec("softmax")
     fn = registry.best("softmax")
-    for shape in [(4, 32768), (4, 1024), (4, 32768), (300, 4095), (4, 32768)]:
+    # rows of 16-bit values from 8K to 32K elements share one kernel instantiation and
+    # need shared-memory stages of different sizes
+    for shape in [(4, 32768), (4, 16384), (4, 32768), (4, 8192), (4, 24576), (4, 32768),
+                  (4, 1024), (300, 4095), (4, 32768)]:
         res = check_impl(spec, "best", fn, shape, torch.bfloat16, "cuda")
         assert res.ok, res.summary()
