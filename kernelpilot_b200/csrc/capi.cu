@@ -106,7 +106,9 @@ int scratch_alloc(void** p, size_t bytes, cudaStream_t s) {
 // dynamic shared-memory opt-in is set once, and occupancy answers are kept. The
 // runtime queries cost tens to hundreds of microseconds of host time per call.
 namespace {
-using LaunchKey = std::tuple<int, const void*, int, size_t, int>;
+enum class Fact { kSmemOptIn, kBlocksPerSm, kClusters };
+// (device, kernel, fact, threads, dynamic shared memory, cluster size)
+using LaunchKey = std::tuple<int, const void*, Fact, int, size_t, int>;
 std::map<LaunchKey, int> g_launch_facts;
 
 int current_device(int* dev) {
@@ -120,7 +122,7 @@ int current_device(int* dev) {
 int ensure_dyn_smem(const void* func, int bytes) {
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
-  const LaunchKey key{dev, func, -1, 0, 0};
+  const LaunchKey key{dev, func, Fact::kSmemOptIn, 0, 0, 0};
   std::lock_guard<std::mutex> lk(g_mu);
   auto it = g_launch_facts.find(key);
   if (it != g_launch_facts.end() && it->second >= bytes) return KPB_OK;
@@ -132,7 +134,7 @@ int ensure_dyn_smem(const void* func, int bytes) {
 int occupancy_blocks(const void* func, int threads, size_t smem, int* out) {
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
-  const LaunchKey key{dev, func, threads, smem, 1};
+  const LaunchKey key{dev, func, Fact::kBlocksPerSm, threads, smem, 0};
   std::lock_guard<std::mutex> lk(g_mu);
   auto it = g_launch_facts.find(key);
   if (it == g_launch_facts.end()) {
@@ -147,8 +149,8 @@ int occupancy_blocks(const void* func, int threads, size_t smem, int* out) {
 int occupancy_clusters(const void* func, const cudaLaunchConfig_t& cfg, int cluster, int* out) {
   int dev = 0;
   if (int rc = current_device(&dev)) return rc;
-  const LaunchKey key{dev, func, static_cast<int>(cfg.blockDim.x), cfg.dynamicSmemBytes,
-                      100 + cluster};
+  const LaunchKey key{dev, func, Fact::kClusters, static_cast<int>(cfg.blockDim.x),
+                      cfg.dynamicSmemBytes, cluster};
   std::lock_guard<std::mutex> lk(g_mu);
   auto it = g_launch_facts.find(key);
   if (it == g_launch_facts.end()) {
