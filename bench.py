@@ -142,9 +142,12 @@ def rounded(d: dict, nd: int = 5) -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
+    """nvidia-smi clock/throttle samples every 50 ms while the timed region runs. The
+    summary keeps the samples taken inside the window given to ``load`` (the steps
+    under load, by the host's clock), or the one nearest to it when the window is
+    shorter than the sampling period."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -152,12 +155,13 @@ class ClockSampler:
         self.gpu_index = gpu_index
         self.proc = None
         self.out = ""
+        self.window = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -165,7 +169,7 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc is not None:
-            time.sleep(0.25)
+            time.sleep(0.1)
             self.proc.terminate()
             try:
                 self.out, _ = self.proc.communicate(timeout=5)
@@ -173,24 +177,40 @@ class ClockSampler:
                 self.proc.kill()
                 self.out, _ = self.proc.communicate()
 
+    def load(self, t0: float, t1: float) -> None:
+        """The wall-clock window (time.time()) in which the GPU ran the steps."""
+        self.window = (t0, t1)
+
     def summary(self) -> dict:
-        sm, smax, reasons = [], None, set()
+        import datetime
+
+        rows = []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in (self.out or "").splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[2]), float(parts[3]),
+                             {n for n, v in zip(names, parts[6:10], strict=False)
+                              if v.lower() == "active"}))
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9], strict=False):
-                if val.lower() == "active":
-                    reasons.add(name)
+        kept = rows
+        if self.window is not None and rows:
+            t0, t1 = self.window
+            kept = [r for r in rows if t0 <= r[0] <= t1]
+            if not kept:
+                mid = (t0 + t1) / 2
+                kept = [min(rows, key=lambda r: abs(r[0] - mid))]
+        sm = [r[1] for r in kept]
+        reasons = set().union(*(r[3] for r in kept)) if kept else set()
         return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_mhz_min": min(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "sm_mhz_min": min(sm) if sm else None,
+                "sm_max_mhz": kept[-1][2] if kept else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "samples_total": len(rows)}
 
 
 def physical_gpu_index(local_rank: int) -> int:
@@ -667,11 +687,13 @@ def main() -> int:
     step = make_step(w, inputs, exchange)
 
     with ClockSampler(physical_gpu_index(rk.local_rank)) as clocks:
+        t_load = time.time()
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
         total_ms, per = time_steps(step, args.steps, flush, rk.world,
                                    align=isinstance(exchange, kdist.PeerSum))
+        clocks.load(t_load, time.time())
     ms = total_ms / args.steps
 
     check = None

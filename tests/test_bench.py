@@ -150,3 +150,30 @@ def test_flush_decision_is_the_same_on_every_rank():
     for p in procs:
         p.join(timeout=60)
     assert got[0] is False and got[1] is False, got  # the larger shard decides
+
+
+def test_clock_summary_keeps_the_samples_of_the_timed_window():
+    import datetime
+
+    import bench
+
+    def line(t, mhz, power_cap="Not Active"):
+        stamp = datetime.datetime.fromtimestamp(t).strftime("%Y/%m/%d %H:%M:%S.%f")[:-3]
+        return (f"{stamp}, 0, {mhz}, 1965, 700.0, 0x0, Not Active, Not Active, Not Active, "
+                f"{power_cap}")
+
+    t0 = 1_800_000_000.0
+    c = bench.ClockSampler(0)
+    c.out = "\n".join([line(t0 - 0.2, 1200), line(t0 + 0.05, 1965),
+                       line(t0 + 0.10, 1900, "Active"), line(t0 + 0.6, 1200)])
+    c.load(t0, t0 + 0.2)
+    got = c.summary()
+    assert got["samples"] == 2 and got["samples_total"] == 4
+    assert got["sm_mhz_min"] == 1900 and got["sm_max_mhz"] == 1965
+    assert got["reasons"] == ["sw_power_cap"]
+    # a window shorter than the sampling period keeps the nearest sample
+    c.load(t0 + 0.55, t0 + 0.56)
+    assert c.summary()["samples"] == 1 and c.summary()["sm_mhz"] == 1200
+    # no window: every sample
+    c.window = None
+    assert c.summary()["samples"] == 4
